@@ -1,0 +1,97 @@
+// tiny_llm::KVCacheManager over the B200 paged KV cache (C-ABI tllm_kv.h).
+//
+// Keeps every signature of the reference class (include/tiny_llm/kv_cache.h:
+// 24-111 in AICL-Lab/tiny-llm): create / allocateSequence / releaseSequence /
+// getCache / getCacheChecked / appendKV / advanceSeqLen / getSeqLen /
+// hasSequence / memory statistics / getActiveSequenceCount / getConfig, the
+// non-copyable, non-movable ownership and the error texts. It adds the paged
+// and fused entry points (reserve, appendKVAllLayers, decodeAttention,
+// getBlockTable, getPoolStats).
+//
+// Behavioural differences, by design:
+//  - memory is a pool of fixed-size blocks; a sequence takes one block at
+//    allocation and more as it grows, so getUsedMemory() counts blocks;
+//  - getCache() points at the sequence's first block of the layer, which
+//    (token-major layout) holds tokens 0..block_size-1 as [pos][Hkv][D];
+//  - CUDA failures are returned as errors instead of thrown.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <memory>
+#include <utility>
+#include <vector>
+
+#include "tiny_llm/result.h"
+#include "tllm_kv.h"
+
+namespace tiny_llm {
+
+// Reference KVCacheConfig (include/tiny_llm/types.h:122-128) plus the paged
+// pool and RoPE settings. num_heads is the KV-head count, as the reference
+// engine passes it (src/inference_engine.cpp:59).
+struct KVCacheConfig {
+    int num_layers = 32;
+    int num_heads = 32;
+    int head_dim = 128;
+    int max_seq_len = 2048;
+    int max_batch_size = 1;
+    int block_size = 16;
+    long long num_blocks = 0;  // 0: max_batch_size * ceil(max_seq_len / block_size)
+    int num_q_heads = 0;       // 0: num_heads (MHA)
+    float rope_theta = 10000.0f;
+    bool rope_on_append = false;
+    int layout = TL_LAYOUT_TOKEN_MAJOR;
+    int backend = TL_BACKEND_CUDA;
+    int device = -1;
+};
+
+class KVCacheManager {
+  public:
+    static Result<std::unique_ptr<KVCacheManager>> create(const KVCacheConfig &config);
+    ~KVCacheManager();
+
+    KVCacheManager(const KVCacheManager &) = delete;
+    KVCacheManager &operator=(const KVCacheManager &) = delete;
+    KVCacheManager(KVCacheManager &&) = delete;
+    KVCacheManager &operator=(KVCacheManager &&) = delete;
+
+    Result<int> allocateSequence(int max_len);
+    Result<void> releaseSequence(int seq_id);
+    std::pair<half *, half *> getCache(int seq_id, int layer_idx);
+    Result<std::pair<half *, half *>> getCacheChecked(int seq_id, int layer_idx);
+    Result<void> appendKV(int seq_id, int layer_idx, const half *new_k, const half *new_v,
+                          int num_tokens, cudaStream_t stream = 0);
+    Result<void> advanceSeqLen(int seq_id, int num_tokens);
+    int getSeqLen(int seq_id) const noexcept;
+    bool hasSequence(int seq_id) const noexcept;
+    size_t getUsedMemory() const noexcept;
+    size_t getTotalMemory() const noexcept;
+    size_t getFreeMemory() const noexcept;
+    int getActiveSequenceCount() const noexcept;
+    const KVCacheConfig &getConfig() const noexcept { return config_; }
+
+    // Paged / fused additions.
+    Result<void> reserve(int seq_id, int new_len);
+    Result<void> appendKVAllLayers(const std::vector<int> &seq_ids, const half *k, const half *v,
+                                   cudaStream_t stream = 0);
+    // Replacement of kernels::attention_decode for TransformerLayer::attention.
+    Result<void> decodeAttention(int layer_idx, const half *q, half *out,
+                                 const std::vector<int> &seq_ids, float scale = 0.0f,
+                                 cudaStream_t stream = 0);
+    Result<std::vector<int>> getBlockTable(int seq_id) const;
+    tl_pool_stats getPoolStats() const noexcept;
+    Result<void> syncCheck(cudaStream_t stream = 0);
+    tl_cache *handle() noexcept { return h_; }
+
+  private:
+    explicit KVCacheManager(const KVCacheConfig &config) : config_(config) {}
+    Result<void> status(int code) const;
+
+    KVCacheConfig config_;
+    tl_cache *h_ = nullptr;
+};
+
+}  // namespace tiny_llm

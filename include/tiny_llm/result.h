@@ -1,0 +1,66 @@
+// Result<T>: value-or-message return type of the tiny_llm C++ API.
+//
+// Interface kept alike with the reference's include/tiny_llm/result.h:11-112
+// (ok/err factories, isOk/isErr, value() that throws on error, error() that
+// throws on ok, valueOr, and a Result<void> specialisation) so code written
+// against tiny-llm's KVCacheManager compiles unchanged.
+#pragma once
+
+#include <stdexcept>
+#include <string>
+#include <utility>
+#include <variant>
+
+namespace tiny_llm {
+
+template <typename T>
+class Result {
+  public:
+    using ValueType = T;
+
+    static Result ok(T value) { return Result(std::in_place_index<0>, std::move(value)); }
+    static Result err(std::string message) { return Result(std::in_place_index<1>, std::move(message)); }
+
+    bool isOk() const { return state_.index() == 0; }
+    bool isErr() const { return !isOk(); }
+
+    T &value() {
+        if (isErr()) throw std::runtime_error("Attempted to access value of error Result: " + error());
+        return std::get<0>(state_);
+    }
+    const T &value() const {
+        if (isErr()) throw std::runtime_error("Attempted to access value of error Result: " + error());
+        return std::get<0>(state_);
+    }
+    const std::string &error() const {
+        if (isOk()) throw std::runtime_error("Attempted to access error of ok Result");
+        return std::get<1>(state_);
+    }
+    T valueOr(T fallback) const { return isOk() ? std::get<0>(state_) : std::move(fallback); }
+
+  private:
+    template <std::size_t I, typename U>
+    Result(std::in_place_index_t<I> tag, U &&u) : state_(tag, std::forward<U>(u)) {}
+    std::variant<T, std::string> state_;
+};
+
+template <>
+class Result<void> {
+  public:
+    static Result ok() { return Result(true, std::string()); }
+    static Result err(std::string message) { return Result(false, std::move(message)); }
+
+    bool isOk() const { return ok_; }
+    bool isErr() const { return !ok_; }
+    const std::string &error() const {
+        if (ok_) throw std::runtime_error("Attempted to access error of ok Result");
+        return message_;
+    }
+
+  private:
+    Result(bool ok, std::string m) : ok_(ok), message_(std::move(m)) {}
+    bool ok_;
+    std::string message_;
+};
+
+}  // namespace tiny_llm

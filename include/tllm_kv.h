@@ -1,0 +1,202 @@
+/*
+ * tllm_kv.h — C-ABI of the B200 paged KV cache and GQA decode attention.
+ *
+ * This is the drop-in boundary for the hot path of AICL-Lab/tiny-llm:
+ *   - the KVCacheManager API (include/tiny_llm/kv_cache.h:24-111 in the
+ *     reference), re-implemented over a block pool with per-sequence block
+ *     tables, and
+ *   - the decode-attention call TransformerLayer::attention makes
+ *     (kernels/attention.cuh:15-18, called at src/transformer.cpp:230-237).
+ * The C++ facade tiny_llm::KVCacheManager (include/tiny_llm/kv_cache.h of
+ * this repository) keeps the reference's C++ signatures on top of it.
+ *
+ * Conventions
+ *   - Every function returns an int status (TL_OK = 0, negative = error) and
+ *     never throws. The message of the last error on a handle is returned by
+ *     tl_last_error(handle); tl_last_error(NULL) gives the last error of a
+ *     failed tl_create on the calling thread.
+ *   - Device pointers (K/V/Q/O) are owned by the caller; the pool, the block
+ *     tables, the RoPE table and the split-K scratch are owned by the handle.
+ *   - All device work is ordered on the caller's stream; no call blocks on
+ *     the device except tl_sync_check and tl_destroy.
+ *   - A handle is not thread-safe: one handle per GPU (per rank), driven from
+ *     one host thread, as in the reference.
+ *   - fp16 tensors are IEEE binary16 (the reference's `half`).
+ */
+#ifndef TLLM_KV_H
+#define TLLM_KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t, without pulling in the CUDA headers. */
+typedef struct CUstream_st *tl_stream_t;
+typedef struct tl_cache tl_cache;
+
+enum tl_status {
+    TL_OK = 0,
+    TL_ERR_INVALID_ARG = -1, /* bad pointer, size, layer index, ... */
+    TL_ERR_NOT_FOUND = -2,   /* unknown sequence id ("not found") */
+    TL_ERR_EXHAUSTED = -3,   /* no free sequence slot or no free block ("exhausted") */
+    TL_ERR_OVERFLOW = -4,    /* append past the sequence's max_len ("overflow") */
+    TL_ERR_CUDA = -5,        /* a CUDA runtime call failed */
+    TL_ERR_NO_DEVICE = -6,   /* compute call on a handle without a CUDA device */
+    TL_ERR_UNSUPPORTED = -7, /* shape outside what the kernels are built for */
+    TL_ERR_DEVICE_FAULT = -8 /* a kernel reported a bounds/timeout error word */
+};
+
+enum tl_backend {
+    TL_BACKEND_CUDA = 0,
+    /* Bookkeeping only: the pool lives in host memory and every call that
+     * would launch a kernel returns TL_ERR_NO_DEVICE. For testing the
+     * allocator and the manager semantics on machines without a GPU. */
+    TL_BACKEND_HOST_BOOKKEEPING = 1
+};
+
+enum tl_layout {
+    /* block = [block_size][Hkv][D]: the first block of a layer holds tokens
+     * 0..block_size-1 exactly as the reference's contiguous [pos][Hkv][D]
+     * region (src/kv_cache.cpp:226), so tl_get_cache() readers keep working. */
+    TL_LAYOUT_TOKEN_MAJOR = 0,
+    /* block = [Hkv][block_size][D]: each (block, head) is one contiguous run. */
+    TL_LAYOUT_HEAD_MAJOR = 1
+};
+
+/* Reference KVCacheConfig (include/tiny_llm/types.h:122-128) plus the paged
+ * pool and RoPE fields. Zero-valued optional fields take the noted default. */
+typedef struct {
+    int num_layers;     /* L */
+    int num_kv_heads;   /* Hkv (the reference's KVCacheConfig::num_heads) */
+    int head_dim;       /* D: 64, 128 or 256 */
+    int max_seq_len;    /* per-sequence cap on max_len */
+    int max_batch_size; /* max concurrently allocated sequences */
+    int block_size;     /* tokens per block; 0 -> 16. Must be 16 or 32 */
+    long long num_blocks; /* pool blocks; 0 -> max_batch_size*ceil(max_seq_len/block_size) */
+    int num_q_heads;    /* Hq for decode (multiple of Hkv); 0 -> num_kv_heads */
+    float rope_theta;   /* RoPE base; used when rope_on_append != 0 */
+    int rope_on_append; /* 1: rotate K (rotate-half) at its position while appending */
+    int layout;         /* enum tl_layout */
+    int backend;        /* enum tl_backend */
+    int device;         /* CUDA device ordinal; -1 -> current device */
+} tl_config;
+
+typedef struct {
+    long long num_blocks;      /* pool capacity in blocks */
+    long long used_blocks;     /* blocks held by live sequences */
+    long long free_blocks;     /* blocks on the free list */
+    long long high_water;      /* max used_blocks seen */
+    long long block_bytes;     /* bytes of one block over all layers, K and V */
+    int active_sequences;
+    int max_blocks_per_seq;
+} tl_pool_stats;
+
+/* Fills *cfg with the defaults (reference KVCacheConfig defaults: 32 layers,
+ * 32 heads, head_dim 128, max_seq_len 2048, batch 1; block 16; theta 1e4). */
+void tl_config_init(tl_config *cfg);
+
+/* KVCacheManager::create (reference include/tiny_llm/kv_cache.h:28,
+ * src/kv_cache.cpp:8-59): validates, sizes and allocates the pool and zeroes
+ * it. Errors: TL_ERR_INVALID_ARG ("invalid configuration"), TL_ERR_OVERFLOW
+ * ("overflow"), TL_ERR_CUDA (allocation failed). */
+int tl_create(const tl_config *cfg, tl_cache **out);
+/* ~KVCacheManager (src/kv_cache.cpp:62-67). Synchronizes the device. */
+void tl_destroy(tl_cache *cache);
+
+const char *tl_last_error(const tl_cache *cache);
+const char *tl_status_name(int status);
+
+/* allocateSequence (kv_cache.h:42, kv_cache.cpp:91-119): max_len must be in
+ * 1..max_seq_len ("Invalid max_len"); ids are monotonic and never reused.
+ * Takes one block eagerly; more blocks are taken as the sequence grows. */
+int tl_allocate_sequence(tl_cache *cache, int max_len, int *seq_id);
+/* releaseSequence (kv_cache.h:46, kv_cache.cpp:121-137): returns the
+ * sequence's blocks to the free list. */
+int tl_release_sequence(tl_cache *cache, int seq_id);
+/* Growth: makes sure blocks exist for the first new_len tokens (new_len <=
+ * max_len). No reference counterpart; the reference reserves max_seq_len. */
+int tl_reserve(tl_cache *cache, int seq_id, int new_len);
+
+/* getCacheChecked (kv_cache.h:54, kv_cache.cpp:139-157): K and V base
+ * pointers of the sequence's first block in layer `layer`. With the
+ * token-major layout they address tokens 0..block_size-1 as [pos][Hkv][D]. */
+int tl_get_cache(tl_cache *cache, int seq_id, int layer, void **k, void **v);
+
+/* appendKV (kv_cache.h:61-62, kv_cache.cpp:168-238): writes num_tokens rows
+ * k/v [num_tokens][Hkv][D] (device, fp16) of one layer at positions
+ * current_len.. of the sequence, growing its block list as needed; K is
+ * rotated by RoPE when the handle was created with rope_on_append. Does not
+ * advance the visible length. Errors: "is null", "num_tokens must be
+ * positive", "Invalid layer_idx", "not found", "overflow", "exhausted". */
+int tl_append_kv(tl_cache *cache, int seq_id, int layer, const void *k, const void *v,
+                 int num_tokens, tl_stream_t stream);
+
+/* Fused decode append: one token per sequence for every layer in ONE kernel.
+ * k/v: [L][num_seqs][Hkv][D] fp16 on the device; seq_ids: host array. Each
+ * token goes to position current_len of its sequence. */
+int tl_append_kv_all_layers(tl_cache *cache, const int *seq_ids, int num_seqs, const void *k,
+                            const void *v, tl_stream_t stream);
+
+/* advanceSeqLen (kv_cache.h:67, kv_cache.cpp:240-259): current_len =
+ * min(current_len + n, max_len); n <= 0 is an error and changes nothing. */
+int tl_advance_seq_len(tl_cache *cache, int seq_id, int num_tokens);
+
+/* getSeqLen / hasSequence / memory statistics / getActiveSequenceCount
+ * (kv_cache.h:70-84). Memory figures count whole blocks. */
+int tl_get_seq_len(const tl_cache *cache, int seq_id);
+int tl_has_sequence(const tl_cache *cache, int seq_id);
+size_t tl_used_memory(const tl_cache *cache);
+size_t tl_total_memory(const tl_cache *cache);
+size_t tl_free_memory(const tl_cache *cache);
+int tl_active_sequence_count(const tl_cache *cache);
+int tl_get_config(const tl_cache *cache, tl_config *cfg);
+
+/* Block table of a sequence (host copy): writes up to cap block ids. */
+int tl_get_block_table(const tl_cache *cache, int seq_id, int *blocks, int cap, int *count);
+int tl_get_pool_stats(const tl_cache *cache, tl_pool_stats *stats);
+
+/* Device base of the pool [L][2][num_blocks][block] and the element count,
+ * for inspection tools and tests. */
+int tl_get_pool(const tl_cache *cache, void **base, size_t *elements);
+
+/* Replacement for kernels::attention_decode (kernels/attention.cuh:15-18) as
+ * called from TransformerLayer::attention (src/transformer.cpp:230-237):
+ * GQA decode attention of layer `layer` for num_seqs sequences over their
+ * paged K/V. q: [num_seqs][Hq][D] fp16 (device), o: [num_seqs][Hq][D] fp16
+ * (device), seq_ids: host array. Each sequence attends to its written
+ * tokens: current_len + the tokens appended since the last advance (the
+ * reference's getSeqLen()+1 in decode). A sequence with no tokens gets
+ * zeros. scale <= 0 -> 1/sqrt(D). Split-K with a merge pass over the
+ * handle's scratch. */
+int tl_decode_attention(tl_cache *cache, int layer, const void *q, void *o, const int *seq_ids,
+                        int num_seqs, float scale, tl_stream_t stream);
+
+/* Synchronizes `stream`, then reads and clears the handle's device error
+ * word; returns TL_ERR_DEVICE_FAULT (with a message) if a kernel recorded
+ * an out-of-range block/position or a wait that gave up. */
+int tl_sync_check(tl_cache *cache, tl_stream_t stream);
+
+/* Host-side RoPE table with the same math the handle uploads:
+ * freq_i = theta^(-2i/D) in double, cos/sin(pos*freq_i) in double, rounded
+ * to float; cos_t/sin_t are [max_pos][D/2]. Useful for rotating Q. */
+void tl_rope_table(float *cos_t, float *sin_t, int max_pos, int head_dim, float theta);
+
+/* Shuffles the free list so later allocations hand out blocks in a random
+ * order (the ragged benchmark's "block tables randomly permuted over a
+ * shared pool"). No reference counterpart. */
+int tl_permute_free_blocks(tl_cache *cache, unsigned long long seed);
+
+/* Testing hook: the nth storage allocation from now fails as if cudaMalloc
+ * had failed (0 disables). Used by the failure-path tests. */
+int tl_debug_inject_alloc_failure(int nth);
+
+/* Library version string. */
+const char *tl_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

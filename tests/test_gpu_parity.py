@@ -1,0 +1,152 @@
+"""Parity of the CUDA path (through the C-ABI) with the CPU oracle.
+
+Append / block-table gathers: bit-exact. Decode attention: elementwise
+|got - ref| <= 2e-3 + 1e-3*|ref| against the fp64 restatement of the
+reference kernel's math (kernels/attention.cu:34-111) generalised to GQA.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import conftest
+import oracle as O
+import tiny_llm_b200 as T
+from gpu_helpers import Run, check_close, d2h, from_dev, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _need_gpu():
+    if not conftest.cuda_available():
+        pytest.skip("no CUDA device")
+
+
+@pytest.mark.parametrize("rope", [False, True])
+@pytest.mark.parametrize("layout", [T.TL_LAYOUT_TOKEN_MAJOR, T.TL_LAYOUT_HEAD_MAJOR])
+def test_config1_tiny_gqa_end_to_end(rope, layout):
+    """L=2, Hq=8, Hkv=2, D=64, bs=16, prompts {17,64,100,128},
+    then 32 decode steps (fused append + decode per layer + advance)."""
+    r = Run.create(L=2, Hq=8, Hkv=2, D=64, bs=16, max_seq_len=256, max_batch=4, rope=rope,
+                   layout=layout)
+    prompts = [17, 64, 100, 128]
+    sids = [r.allocate(P + 32) for P in prompts]
+    for i, (sid, P) in enumerate(zip(sids, prompts)):
+        r.prefill(sid, P, seed=10 + i)
+    r.check_pool_bit_exact()
+    for step in range(32):
+        r.step_append(sids, seed=5000 + 7 * step)
+        for layer in range(2):
+            r.decode_and_check(layer, sids, seed=9000 + 3 * step + layer)
+        for sid in sids:
+            r.cache.advance_seq_len(sid, 1)
+    r.check_pool_bit_exact()
+    for sid, P in zip(sids, prompts):
+        assert r.cache.get_seq_len(sid) == P + 32
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("G", [1, 4, 8])
+@pytest.mark.parametrize("bs", [16, 32])
+def test_decode_shapes(D, G, bs):
+    Hkv = 2
+    r = Run.create(L=1, Hq=Hkv * G, Hkv=Hkv, D=D, bs=bs, max_seq_len=700, max_batch=5,
+                   rope=(G == 4), permute_seed=3)
+    lens = [1, 16, 33, 300, 640]
+    sids = [r.allocate(700) for _ in lens]
+    for i, (sid, S) in enumerate(zip(sids, lens)):
+        r.prefill(sid, S, seed=100 + i)
+    r.check_pool_bit_exact()
+    r.decode_and_check(0, sids, seed=77)
+
+
+def test_single_long_sequence_many_splits():
+    """One KV head, one long sequence: every worker gets a slice of the same
+    unit, so the merge pass combines hundreds of partials."""
+    r = Run.create(L=1, Hq=8, Hkv=1, D=128, bs=16, max_seq_len=9000, max_batch=1)
+    sid = r.allocate(9000)
+    r.prefill(sid, 8999, seed=5)
+    r.decode_and_check(0, [sid], seed=6)
+
+
+def test_ragged_permuted_batch_and_subsets():
+    r = Run.create(L=2, Hq=32, Hkv=8, D=128, bs=16, max_seq_len=1200, max_batch=12,
+                   permute_seed=42)
+    rng = np.random.default_rng(0)
+    lens = rng.integers(1, 1100, size=12)
+    sids = [r.allocate(1200) for _ in lens]
+    for i, (sid, S) in enumerate(zip(sids, lens)):
+        r.prefill(sid, int(S), seed=300 + i)
+    r.check_pool_bit_exact()
+    r.decode_and_check(1, sids, seed=1)
+    r.decode_and_check(0, sids[::3], seed=2)            # a subset, out of order
+    r.decode_and_check(0, [sids[5], sids[5]], seed=3)   # duplicates are fine for decode
+
+
+def test_empty_sequence_decodes_to_zero_and_others_unaffected():
+    r = Run.create(L=1, Hq=4, Hkv=1, D=64, bs=16, max_seq_len=64, max_batch=3)
+    a = r.allocate(64)
+    b = r.allocate(64)
+    r.prefill(b, 20, seed=1)
+    r.decode_and_check(0, [a, b], seed=2)
+
+
+def test_append_then_decode_sees_pending_token():
+    """Reference decode semantics (src/transformer.cpp:230-237): after
+    appendKV and before advanceSeqLen the decode covers getSeqLen()+1."""
+    r = Run.create(L=1, Hq=8, Hkv=2, D=64, bs=16, max_seq_len=64, max_batch=1)
+    s = r.allocate(64)
+    r.prefill(s, 16, seed=1)
+    k = O.normal_f16((1, 2, 64), 50)
+    v = O.normal_f16((1, 2, 64), 51)
+    kd, vd = to_dev(k), to_dev(v)
+    r.cache.append_kv(s, 0, kd.data_ptr(), vd.data_ptr(), 1)
+    r._record(s, 0, 16, k, v)
+    assert r.cache.get_seq_len(s) == 16
+    r.decode_and_check(0, [s], seed=3)  # attends 17 tokens
+    r.cache.advance_seq_len(s, 1)
+    assert r.cache.get_seq_len(s) == 17
+
+
+def test_reference_append_retrieve_contiguous_get_cache():
+    """tests/test_transformer.cu:141-194: 4 tokens x 4 heads x 32 read back
+    contiguously from the getCache pointer (token-major first block)."""
+    c = T.KVCache(num_layers=2, num_kv_heads=4, head_dim=32, max_seq_len=64, max_batch_size=2)
+    s = c.allocate_sequence(32)
+    k = O.normal_f16((4, 4, 32), 200)
+    v = O.normal_f16((4, 4, 32), 201)
+    kd, vd = to_dev(k), to_dev(v)
+    c.append_kv(s, 0, kd.data_ptr(), vd.data_ptr(), 4)
+    c.sync_check()
+    assert c.get_seq_len(s) == 0
+    c.advance_seq_len(s, 4)
+    assert c.get_seq_len(s) == 4
+    kp, vp = c.get_cache(s, 0)
+    assert np.array_equal(d2h(kp, k.size).reshape(k.shape), k)
+    assert np.array_equal(d2h(vp, v.size).reshape(v.shape), v)
+
+
+def test_block_exhaustion_on_device_keeps_state():
+    c = T.KVCache(num_layers=1, num_kv_heads=1, head_dim=64, max_seq_len=64, max_batch_size=2,
+                  num_blocks=3)
+    a = c.allocate_sequence(64)
+    c.allocate_sequence(64)
+    k = to_dev(O.normal_f16((40, 1, 64), 1))
+    with pytest.raises(T.Exhausted):
+        c.append_kv(a, 0, k.data_ptr(), k.data_ptr(), 40)
+    assert c.get_seq_len(a) == 0 and len(c.block_table(a)) == 1
+    c.sync_check()
+
+
+def test_all_layer_append_rejects_duplicates_and_overflow():
+    c = T.KVCache(num_layers=2, num_kv_heads=1, head_dim=64, max_seq_len=4, max_batch_size=2)
+    a = c.allocate_sequence(1)
+    k = to_dev(O.normal_f16((2, 2, 1, 64), 1))
+    with pytest.raises(T.InvalidArgument):
+        c.append_kv_all_layers([a, a], k.data_ptr(), k.data_ptr())
+    c.append_kv_all_layers([a], k.data_ptr(), k.data_ptr())
+    c.advance_seq_len(a, 1)
+    with pytest.raises(T.Overflow):
+        c.append_kv_all_layers([a], k.data_ptr(), k.data_ptr())
+    c.sync_check()

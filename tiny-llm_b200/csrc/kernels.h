@@ -1,0 +1,100 @@
+// Launch interface between the host manager (paged_kv.cpp) and the sm_100a
+// kernels (kv_append.cu, paged_decode.cu). Argument blocks are passed to the
+// kernels by value, so every per-call array here is bounded to keep a launch
+// under the 4 KiB classic kernel-parameter limit; the host splits larger
+// batches into several launches.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace tllm {
+
+// Device error word bits (atomicOr'd by kernels, read by tl_sync_check).
+enum DeviceErrorBits : int {
+    kErrBlockRange = 1 << 0,   // a block id outside [0, num_blocks)
+    kErrPosRange = 1 << 1,     // a position outside the RoPE table / sequence
+    kErrWaitTimeout = 1 << 2,  // an mbarrier wait gave up (bounded spin)
+};
+
+constexpr int kMaxAppendRows = 256;
+constexpr int kMaxDeltas = 96;
+constexpr int kMaxDecodeSeqs = 256;
+
+// Pool geometry shared by every kernel.
+struct PoolGeom {
+    void *pool;             // fp16 [L][2][num_blocks][block]
+    long long num_blocks;   // NB
+    int num_layers;         // L
+    int num_kv_heads;       // Hkv
+    int head_dim;           // D
+    int block_size;         // bs
+    int head_major;         // 0: block = [bs][Hkv][D]; 1: [Hkv][bs][D]
+    int bt_stride;          // ints per block-table row (max blocks per sequence)
+    int *block_tables;      // device [max_batch][bt_stride]
+    int *err;               // device error word
+};
+
+// One append launch: `nrows` token rows for `num_layers` consecutive layers.
+struct AppendArgs {
+    PoolGeom g;
+    const void *k;          // fp16 rows of [Hkv][D]
+    const void *v;
+    const float *rope_cos;  // [rope_max_pos][D/2] or nullptr (no RoPE)
+    const float *rope_sin;
+    int rope_max_pos;
+    int layer0;             // first destination layer
+    int num_layers;         // layers written (grid.y)
+    int nrows;              // rows in this launch (grid.x)
+    long long src_layer_stride;  // elements between layers in k/v
+    long long src_row_stride;    // elements between rows in k/v
+    int ndeltas;            // block-table updates applied by block (0,0)
+    int delta_slot[kMaxDeltas];
+    int delta_idx[kMaxDeltas];
+    int delta_block[kMaxDeltas];
+    int row_block[kMaxAppendRows];  // destination block of each row
+    int row_pos[kMaxAppendRows];    // token position of each row
+};
+
+// Block-table updates alone (used when a decode finds updates pending).
+struct DeltaArgs {
+    int *block_tables;
+    int bt_stride;
+    int ndeltas;
+    int delta_slot[kMaxDeltas];
+    int delta_idx[kMaxDeltas];
+    int delta_block[kMaxDeltas];
+};
+
+// One decode launch over up to kMaxDecodeSeqs sequences of one layer.
+// Work = (sequence, kv_head, block) items ordered sequence-major, then
+// kv_head, then block; worker w (one warp) owns the contiguous item range
+// [w*W/V, (w+1)*W/V) (stream-K split), W = total items, V = workers.
+struct DecodeArgs {
+    PoolGeom g;
+    const void *q;          // fp16 [nseq][Hq][D]
+    void *o;                // fp16 [nseq][Hq][D]
+    float *partial;         // [V][2][G][D+2] fp32 split partials
+    int layer;
+    int group;              // G = Hq / Hkv
+    float scale_log2;       // softmax scale * log2(e)
+    int nseq;
+    long long total_items;  // W
+    int workers;            // V
+    int slot[kMaxDecodeSeqs];     // block-table row of each sequence
+    int len[kMaxDecodeSeqs];      // attended tokens of each sequence
+    int prefix[kMaxDecodeSeqs + 1];  // prefix sums of blocks per sequence
+};
+
+// Sizes the kernels need from the host.
+int decode_workers_per_cta();
+int decode_max_workers(int device, int head_dim, int block_size);
+
+cudaError_t launch_append(const AppendArgs &a, cudaStream_t s);
+cudaError_t launch_apply_deltas(const DeltaArgs &a, cudaStream_t s);
+// Encodes the tensor map once per pool (stored opaque, 128 bytes).
+cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128);
+cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t s);
+cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s);
+
+}  // namespace tllm

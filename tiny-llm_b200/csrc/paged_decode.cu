@@ -1,0 +1,554 @@
+// Split-K (flash-decoding) GQA decode attention over the paged KV pool, and
+// the merge pass, for sm_100a.
+//
+// Replaces kernels::attention_decode (reference kernels/attention.cu:11-128),
+// which runs one CTA per (batch, head) over a contiguous [H][S][D] cache,
+// keeps every score in shared memory and re-reads K/V once per query head.
+//
+// Work decomposition (stream-K). The work of one call is the list of items
+// (sequence b, kv_head h, tile t) in sequence-major order, one item = 16
+// tokens of one KV head. Each WARP is an independent worker that owns one
+// contiguous slice of that list, so every worker gets the same number of
+// tiles whatever the sequence lengths (ragged batches stay balanced). A
+// (sequence, kv_head) unit that a worker covers completely is finished in
+// registers and written as fp16; a unit cut by a worker boundary leaves a
+// partial (m, l, acc) in the split scratch, which the merge kernel combines.
+//
+// Data movement. Each worker owns a ring of NS stages in shared memory.
+// Lane 0 issues TMA tile loads (cp.async.bulk.tensor, no multicast) for the
+// K and V rows of the next tiles, addressed through the block table, with
+// an evict-first L2 policy; an mbarrier per stage signals arrival. The tile
+// is stored as 64-element (128-byte) half-rows with the 128-byte swizzle, so
+// the ldmatrix reads below are bank-conflict free.
+//
+// Math (per 16-token tile, per warp). The query group (G <= 8 heads sharing
+// one KV head) is the N=8 side of mma.sync m16n8k16:
+//   S^T[t][g] = K[t][:] . Q[g][:]        (A = K from smem, B = Q in registers)
+//   online softmax over t, per head g, in the exp2 domain (fp32)
+//   O^T[d][g] += V^T[d][t] P^T[t][g]      (A = V^T via ldmatrix.trans,
+//                                           B = P^T via movmatrix.trans)
+// so each K/V tile is read from shared memory once for all G heads. fp16
+// operands, fp32 accumulation, fp32 softmax state.
+//
+// Waits are bounded (globaltimer); a wait that gives up sets an error bit,
+// drains the worker's own in-flight loads (bounded) and stops the worker.
+#include <atomic>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace tllm {
+namespace {
+
+constexpr int kTile = 16;          // tokens per item
+constexpr int kWarps = 4;          // workers per CTA
+constexpr int kSmemBudget = 160 * 1024;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+template <int D>
+struct Cfg {
+    static constexpr int kNSub = D / 64;                  // 128-byte half-row tiles per row
+    static constexpr int kSubBytes = kTile * 128;         // one [16][64] fp16 tile
+    static constexpr int kStageBytes = 2 * kNSub * kSubBytes;  // K + V
+    static constexpr int kNS0 = kSmemBudget / (kWarps * kStageBytes);
+    static constexpr int kNS = kNS0 < 2 ? 2 : (kNS0 > 8 ? 8 : kNS0);
+    static constexpr int kRingBytes = kNS * kStageBytes;
+    static constexpr int kSmemBytes = kWarps * kRingBytes + kWarps * kNS * 8 + 1024;
+    static constexpr int kKS = D / 16;                    // k-steps of the QK mma
+};
+
+struct ItemPos {
+    int b, kvh, tile, nb;
+    long long unit_first;
+};
+
+// Maps a flat item index to (sequence, kv_head, tile). prefix[] lives in the
+// kernel's parameter space; the search is uniform across the warp.
+__device__ __forceinline__ ItemPos locate(const DecodeArgs &a, long long w) {
+    const int H = a.g.num_kv_heads;
+    int lo = 0, hi = a.nseq - 1;
+    while (lo < hi) {  // largest b with H*prefix[b] <= w
+        const int mid = (lo + hi + 1) >> 1;
+        if ((long long)H * a.prefix[mid] <= w) lo = mid;
+        else hi = mid - 1;
+    }
+    ItemPos p;
+    p.b = lo;
+    p.nb = a.prefix[lo + 1] - a.prefix[lo];
+    const int r = (int)(w - (long long)H * a.prefix[lo]);  // < H * nb < 2^31
+    p.kvh = r / p.nb;
+    p.tile = r - p.kvh * p.nb;
+    p.unit_first = (long long)H * a.prefix[lo] + (long long)p.kvh * p.nb;
+    return p;
+}
+
+__device__ __forceinline__ long long worker_start(long long v, long long W, long long V) {
+    return v * W / V;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWarps * 32, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ DecodeArgs a) {
+    using C = Cfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    const long long worker = (long long)blockIdx.x * kWarps + warp;
+    if (worker >= a.workers) return;
+    const long long W = a.total_items, V = a.workers;
+    const long long ws = worker_start(worker, W, V);
+    const long long we = worker_start(worker + 1, W, V);
+    const int count = (int)(we - ws);
+    if (count <= 0) return;
+
+    const PoolGeom &g = a.g;
+    const int H = g.num_kv_heads, G = a.group, Hq = H * G, BS = g.block_size;
+    uint8_t *ring = smem + warp * C::kRingBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWarps * C::kRingBytes) + warp * C::kNS;
+    const uint32_t ring_u32 = ptx::smem_u32(ring);
+    const uint32_t bar_u32 = ptx::smem_u32(bars);
+
+    if (lane == 0) {
+        for (int s = 0; s < C::kNS; ++s) ptx::mbar_init(bar_u32 + 8 * s, 1);
+        ptx::fence_barrier_init();
+    }
+    __syncwarp();
+
+    const uint64_t policy = ptx::l2_policy_evict_first();
+    const long long layer_k_row = (long long)(a.layer * 2 + 0) * g.num_blocks;
+    const long long layer_v_row = (long long)(a.layer * 2 + 1) * g.num_blocks;
+
+    // ---- producer side: lane j of a batch describes item (base + j) ------
+    struct Batch {
+        int bid, kvh, sub;
+    };
+    auto load_batch = [&](long long base) {
+        Batch r{0, 0, 0};
+        const long long w = base + lane;
+        if (w < we) {
+            const ItemPos p = locate(a, w);
+            const int tok0 = p.tile * kTile;
+            const int slot = a.slot[p.b];
+            int bid = __ldg(g.block_tables + (long long)slot * g.bt_stride + tok0 / BS);
+            if (bid < 0 || bid >= g.num_blocks) {
+                atomicOr(g.err, kErrBlockRange);
+                bid = 0;  // stay in bounds; the call reports the error
+            }
+            r.bid = bid;
+            r.kvh = p.kvh;
+            r.sub = tok0 % BS;
+        }
+        return r;
+    };
+    Batch cur = load_batch(ws);
+    Batch nxt = load_batch(ws + 32);
+    int issued = 0;
+    auto issue_one = [&]() {
+        const int j = issued & 31;
+        const int bid = __shfl_sync(0xffffffffu, cur.bid, j);
+        const int kvh = __shfl_sync(0xffffffffu, cur.kvh, j);
+        const int sub = __shfl_sync(0xffffffffu, cur.sub, j);
+        if (lane == 0) {
+            const int stage = issued % C::kNS;
+            const uint32_t bar = bar_u32 + 8 * stage;
+            const uint32_t dst = ring_u32 + stage * C::kStageBytes;
+            ptx::fence_proxy_async_smem();
+            ptx::mbar_arrive_expect_tx(bar, C::kStageBytes);
+#pragma unroll
+            for (int kv = 0; kv < 2; ++kv) {
+                const long long blk_row = (kv == 0 ? layer_k_row : layer_v_row) + bid;
+                int y, z;
+                if (g.head_major) {
+                    y = sub;
+                    z = (int)(blk_row * H + kvh);
+                } else {
+                    y = kvh;
+                    z = (int)(blk_row * BS + sub);
+                }
+#pragma unroll
+                for (int hs = 0; hs < C::kNSub; ++hs)
+                    ptx::tma_load_3d(dst + (kv * C::kNSub + hs) * C::kSubBytes, &tmap, bar, hs * 64,
+                                     y, z, policy);
+            }
+        }
+        ++issued;
+        if ((issued & 31) == 0) {
+            cur = nxt;
+            nxt = load_batch(ws + issued + 32);
+        }
+    };
+
+    const int prologue = count < C::kNS ? count : C::kNS;
+    for (int i = 0; i < prologue; ++i) issue_one();
+
+    // ---- consumer state for the current (sequence, kv_head) unit ---------
+    uint32_t qf[C::kKS][2];
+    float acc[C::kKS][4];  // O^T tiles: d in [16*dm, 16*dm+16), g in {2tig, 2tig+1}
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    int ub = -1, ukvh = -1, unb = 0;
+    long long ufirst = 0;
+    bool first_piece = true;
+    bool failed = false;
+
+    // Writes the finished unit (complete -> fp16 output; cut -> partial).
+    auto finalize = [&]() {
+        float lt0 = l0, lt1 = l1;
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            lt0 += __shfl_xor_sync(0xffffffffu, lt0, off);
+            lt1 += __shfl_xor_sync(0xffffffffu, lt1, off);
+        }
+        const bool complete = ufirst >= ws && ufirst + unb <= we;
+        const int g0 = 2 * tig, g1 = 2 * tig + 1;
+        if (complete) {
+            __half *o = static_cast<__half *>(a.o) + ((long long)ub * Hq + (long long)ukvh * G) * D;
+            const float i0 = 1.f / lt0, i1 = 1.f / lt1;
+#pragma unroll
+            for (int dm = 0; dm < C::kKS; ++dm) {
+                const int d = dm * 16 + gid;
+                if (g0 < G) {
+                    o[(long long)g0 * D + d] = __float2half_rn(acc[dm][0] * i0);
+                    o[(long long)g0 * D + d + 8] = __float2half_rn(acc[dm][2] * i0);
+                }
+                if (g1 < G) {
+                    o[(long long)g1 * D + d] = __float2half_rn(acc[dm][1] * i1);
+                    o[(long long)g1 * D + d + 8] = __float2half_rn(acc[dm][3] * i1);
+                }
+            }
+        } else {
+            const int slot = first_piece ? 0 : 1;
+            float *pbase = a.partial + ((worker * 2 + slot) * G) * (long long)(D + 2);
+#pragma unroll
+            for (int dm = 0; dm < C::kKS; ++dm) {
+                const int d = dm * 16 + gid;
+                if (g0 < G) {
+                    pbase[g0 * (D + 2) + d] = acc[dm][0];
+                    pbase[g0 * (D + 2) + d + 8] = acc[dm][2];
+                }
+                if (g1 < G) {
+                    pbase[g1 * (D + 2) + d] = acc[dm][1];
+                    pbase[g1 * (D + 2) + d + 8] = acc[dm][3];
+                }
+            }
+            if (gid == 0) {
+                if (g0 < G) {
+                    pbase[g0 * (D + 2) + D] = m0;
+                    pbase[g0 * (D + 2) + D + 1] = lt0;
+                }
+                if (g1 < G) {
+                    pbase[g1 * (D + 2) + D] = m1;
+                    pbase[g1 * (D + 2) + D + 1] = lt1;
+                }
+            }
+        }
+        first_piece = false;
+    };
+
+    ItemPos p = locate(a, ws);
+    bool new_unit = true;
+    int fail_at = -1;
+    for (int i = 0; i < count; ++i) {
+        if (i > 0) {  // advance (sequence, kv_head, tile) by one item
+            if (++p.tile == p.nb) {
+                p.tile = 0;
+                p.unit_first += p.nb;
+                if (++p.kvh == H) {
+                    p.kvh = 0;
+                    do {
+                        ++p.b;
+                        p.nb = a.prefix[p.b + 1] - a.prefix[p.b];
+                    } while (p.nb == 0);
+                }
+                new_unit = true;
+            }
+        }
+        if (new_unit) {
+            new_unit = false;
+            if (ub >= 0) finalize();
+            ub = p.b;
+            ukvh = p.kvh;
+            unb = p.nb;
+            ufirst = p.unit_first;
+            // Q fragments (B operand, col-major 16x8): rows d, cols g = gid.
+            const __half *qrow = static_cast<const __half *>(a.q) +
+                                 ((long long)p.b * Hq + (long long)p.kvh * G + gid) * D;
+#pragma unroll
+            for (int ks = 0; ks < C::kKS; ++ks) {
+                if (gid < G) {
+                    qf[ks][0] = __ldg(reinterpret_cast<const uint32_t *>(qrow + ks * 16 + 2 * tig));
+                    qf[ks][1] = __ldg(reinterpret_cast<const uint32_t *>(qrow + ks * 16 + 8 + 2 * tig));
+                } else {
+                    qf[ks][0] = 0u;
+                    qf[ks][1] = 0u;
+                }
+            }
+#pragma unroll
+            for (int dm = 0; dm < C::kKS; ++dm) acc[dm][0] = acc[dm][1] = acc[dm][2] = acc[dm][3] = 0.f;
+            m0 = m1 = -INFINITY;
+            l0 = l1 = 0.f;
+        }
+
+        const int stage = i % C::kNS;
+        const uint32_t parity = (uint32_t)((i / C::kNS) & 1);
+        if (!ptx::mbar_wait_bounded(bar_u32 + 8 * stage, parity, kWaitLimitNs)) {
+            if (lane == 0) atomicOr(g.err, kErrWaitTimeout);
+            failed = true;
+            fail_at = i;
+            break;
+        }
+        const uint32_t kbase = ring_u32 + stage * C::kStageBytes;
+        const uint32_t vbase = kbase + C::kNSub * C::kSubBytes;
+        const int nvalid = min(kTile, a.len[p.b] - p.tile * kTile);
+
+        // ---- S^T = K Q^T (two accumulators to shorten the mma chain) ----
+        float s_even[4] = {0.f, 0.f, 0.f, 0.f}, s_odd[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+            const int t = (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int dsel = (lane >> 4) & 1;  // +8 columns
+#pragma unroll
+            for (int ks = 0; ks < C::kKS; ++ks) {
+                const int d = ks * 16 + dsel * 8;
+                const uint32_t addr = kbase + (d >> 6) * C::kSubBytes + t * 128 +
+                                      ((((d & 63) >> 3) ^ (t & 7)) << 4);
+                uint32_t a0, a1, a2, a3;
+                ptx::ldmatrix_x4(addr, a0, a1, a2, a3);
+                if (ks & 1) ptx::mma_16816(s_odd, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+                else ptx::mma_16816(s_even, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+            }
+        }
+        // s[0],s[1]: token gid, heads 2tig, 2tig+1; s[2],s[3]: token gid+8.
+        float s[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) s[r] = (s_even[r] + s_odd[r]) * a.scale_log2;
+        if (gid >= nvalid) s[0] = s[1] = -INFINITY;
+        if (gid + 8 >= nvalid) s[2] = s[3] = -INFINITY;
+
+        // ---- online softmax (exp2 domain) ----
+        float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float al0 = ptx::ex2(m0 - mn0), al1 = ptx::ex2(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        const float p0 = ptx::ex2(s[0] - mn0), p1 = ptx::ex2(s[1] - mn1);
+        const float p2 = ptx::ex2(s[2] - mn0), p3 = ptx::ex2(s[3] - mn1);
+        l0 = l0 * al0 + p0 + p2;
+        l1 = l1 * al1 + p1 + p3;
+#pragma unroll
+        for (int dm = 0; dm < C::kKS; ++dm) {
+            acc[dm][0] *= al0;
+            acc[dm][1] *= al1;
+            acc[dm][2] *= al0;
+            acc[dm][3] *= al1;
+        }
+        const uint32_t pb0 = ptx::movmatrix_trans(ptx::pack_half2(p0, p1));
+        const uint32_t pb1 = ptx::movmatrix_trans(ptx::pack_half2(p2, p3));
+
+        // Rows past the sequence end may hold stale data (even Inf/NaN bit
+        // patterns); zero them so 0 * V stays 0.
+        if (nvalid < kTile) {
+            const int nz = (kTile - nvalid) * C::kNSub * 8;  // 16-byte chunks
+            for (int c = lane; c < nz; c += 32) {
+                const int sub = c / ((kTile - nvalid) * 8);
+                const int rem = c % ((kTile - nvalid) * 8);
+                const int t = nvalid + rem / 8, ch = rem % 8;
+                uint4 *dst = reinterpret_cast<uint4 *>(ring + stage * C::kStageBytes +
+                                                       C::kNSub * C::kSubBytes + sub * C::kSubBytes +
+                                                       t * 128 + ch * 16);
+                *dst = make_uint4(0u, 0u, 0u, 0u);
+            }
+            __syncwarp();
+        }
+
+        // ---- O^T += V^T P^T ----
+        {
+            const int t = (lane & 7) + ((lane >> 4) & 1) * 8;
+            const int dsel = (lane >> 3) & 1;
+#pragma unroll
+            for (int dm = 0; dm < C::kKS; ++dm) {
+                const int d = dm * 16 + dsel * 8;
+                const uint32_t addr = vbase + (d >> 6) * C::kSubBytes + t * 128 +
+                                      ((((d & 63) >> 3) ^ (t & 7)) << 4);
+                uint32_t a0, a1, a2, a3;
+                ptx::ldmatrix_x4_trans(addr, a0, a1, a2, a3);
+                ptx::mma_16816(acc[dm], a0, a1, a2, a3, pb0, pb1);
+            }
+        }
+        __syncwarp();
+        if (issued < count) issue_one();
+    }
+
+    if (failed) {
+        // Drain this worker's own loads still in flight (bounded) and stop.
+        if (lane == 0) {
+            const uint64_t t0 = ptx::globaltimer_ns();
+            for (int it = fail_at; it < issued; ++it) {
+                const int stage = it % C::kNS;
+                const uint32_t parity = (uint32_t)((it / C::kNS) & 1);
+                while (!ptx::mbar_try_wait(bar_u32 + 8 * stage, parity)) {
+                    if (ptx::globaltimer_ns() - t0 > kWaitLimitNs) break;
+                }
+            }
+        }
+        __syncwarp();
+        return;
+    }
+    if (ub >= 0) finalize();
+}
+
+// Combines the partials of every unit that was cut by a worker boundary.
+// CTA v merges the unit that contains worker v's first item when that unit
+// started in an earlier worker and ends inside worker v (so each cut unit
+// has exactly one merger). Sources are workers v_first..v; a source whose
+// first item lies inside the unit stored it in slot 0, otherwise slot 1.
+template <int D>
+__global__ void __launch_bounds__(128) merge_kernel(const __grid_constant__ DecodeArgs a) {
+    const long long v = blockIdx.x;
+    const long long W = a.total_items, V = a.workers;
+    const long long ws = worker_start(v, W, V), we = worker_start(v + 1, W, V);
+    if (we <= ws) return;
+    const ItemPos p = locate(a, ws);
+    const long long ulast = p.unit_first + p.nb - 1;
+    if (p.unit_first >= ws || ulast >= we) return;
+    const long long v_first = ((p.unit_first + 1) * V + W - 1) / W - 1;
+    const int G = a.group, H = a.g.num_kv_heads, Hq = H * G;
+    __half *o = static_cast<__half *>(a.o) + ((long long)p.b * Hq + (long long)p.kvh * G) * D;
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int gg = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (long long u = v_first; u <= v; ++u) {
+            const int slot = worker_start(u, W, V) >= p.unit_first ? 0 : 1;
+            const float *pb = a.partial + ((u * 2 + slot) * G + gg) * (long long)(D + 2);
+            M = fmaxf(M, pb[D]);
+        }
+        float L = 0.f, O = 0.f;
+        for (long long u = v_first; u <= v; ++u) {
+            const int slot = worker_start(u, W, V) >= p.unit_first ? 0 : 1;
+            const float *pb = a.partial + ((u * 2 + slot) * G + gg) * (long long)(D + 2);
+            const float f = ptx::ex2(pb[D] - M);
+            L += f * pb[D + 1];
+            O += f * pb[d];
+        }
+        o[(long long)gg * D + d] = __float2half_rn(O / L);
+    }
+}
+
+// Opts the kernel into its dynamic shared memory size, once per device.
+template <int D>
+cudaError_t prepare() {
+    static std::atomic<unsigned long long> done_mask{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(paged_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg<D>::kSmemBytes);
+    if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
+
+template <int D>
+cudaError_t launch_decode_t(const DecodeArgs &a, const void *tmap128, cudaStream_t s) {
+    cudaError_t e = prepare<D>();
+    if (e != cudaSuccess) return e;
+    const int ctas = (a.workers + kWarps - 1) / kWarps;
+    paged_decode_kernel<D><<<ctas, kWarps * 32, Cfg<D>::kSmemBytes, s>>>(
+        *static_cast<const CUtensorMap *>(tmap128), a);
+    return cudaGetLastError();
+}
+
+template <int D>
+int max_workers_t(int device) {
+    if (prepare<D>() != cudaSuccess) return 0;
+    int per_sm = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<D>, kWarps * 32,
+                                                      Cfg<D>::kSmemBytes) != cudaSuccess)
+        return 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+    return per_sm * sms * kWarps;
+}
+
+}  // namespace
+
+int decode_workers_per_cta() { return kWarps; }
+
+int decode_max_workers(int device, int head_dim, int block_size) {
+    (void)block_size;
+    switch (head_dim) {
+    case 64: return max_workers_t<64>(device);
+    case 128: return max_workers_t<128>(device);
+    case 256: return max_workers_t<256>(device);
+    default: return 0;
+    }
+}
+
+cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t s) {
+    switch (a.g.head_dim) {
+    case 64: return launch_decode_t<64>(a, tmap128, s);
+    case 128: return launch_decode_t<128>(a, tmap128, s);
+    case 256: return launch_decode_t<256>(a, tmap128, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s) {
+    switch (a.g.head_dim) {
+    case 64: merge_kernel<64><<<a.workers, 128, 0, s>>>(a); break;
+    case 128: merge_kernel<128><<<a.workers, 128, 0, s>>>(a); break;
+    case 256: merge_kernel<256><<<a.workers, 128, 0, s>>>(a); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                         cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const unsigned long long L2 = 2ull * g.num_layers;
+    cuuint64_t dims[3], strides[2];
+    cuuint32_t box[3], estr[3] = {1, 1, 1};
+    dims[0] = (cuuint64_t)g.head_dim;
+    if (g.head_major) {
+        dims[1] = (cuuint64_t)g.block_size;
+        dims[2] = (cuuint64_t)(L2 * (unsigned long long)g.num_blocks * g.num_kv_heads);
+        strides[0] = (cuuint64_t)g.head_dim * 2;
+        strides[1] = (cuuint64_t)g.block_size * g.head_dim * 2;
+        box[0] = 64;
+        box[1] = kTile;
+        box[2] = 1;
+    } else {
+        dims[1] = (cuuint64_t)g.num_kv_heads;
+        dims[2] = (cuuint64_t)(L2 * (unsigned long long)g.num_blocks * g.block_size);
+        strides[0] = (cuuint64_t)g.head_dim * 2;
+        strides[1] = (cuuint64_t)g.num_kv_heads * g.head_dim * 2;
+        box[0] = 64;
+        box[1] = 1;
+        box[2] = kTile;
+    }
+    CUresult r = encode(static_cast<CUtensorMap *>(tmap_out128), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                        g.pool, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace tllm
