@@ -92,6 +92,7 @@ typedef struct {
     long long block_bytes;     /* bytes of one block over all layers, K and V */
     int active_sequences;
     int max_blocks_per_seq;
+    long long kernel_launches; /* kernels this handle has launched so far */
 } tl_pool_stats;
 
 /* Fills *cfg with the defaults (reference KVCacheConfig defaults: 32 layers,

@@ -20,6 +20,8 @@ enum DeviceErrorBits : int {
 constexpr int kMaxAppendRows = 256;
 constexpr int kMaxDeltas = 96;
 constexpr int kMaxDecodeSeqs = 256;
+// Decode work item: 16 tokens of one KV head (a block of 32 is two items).
+constexpr int kDecodeTile = 16;
 
 // Pool geometry shared by every kernel.
 struct PoolGeom {
@@ -83,7 +85,7 @@ struct DecodeArgs {
     int workers;            // V
     int slot[kMaxDecodeSeqs];     // block-table row of each sequence
     int len[kMaxDecodeSeqs];      // attended tokens of each sequence
-    int prefix[kMaxDecodeSeqs + 1];  // prefix sums of blocks per sequence
+    int prefix[kMaxDecodeSeqs + 1];  // prefix sums of 16-token tiles per sequence
 };
 
 // Sizes the kernels need from the host.

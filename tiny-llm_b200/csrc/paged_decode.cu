@@ -44,7 +44,7 @@
 namespace tllm {
 namespace {
 
-constexpr int kTile = 16;          // tokens per item
+constexpr int kTile = kDecodeTile;  // tokens per item
 constexpr int kWarps = 4;          // workers per CTA
 constexpr int kSmemBudget = 160 * 1024;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s

@@ -237,6 +237,7 @@ int flush_deltas(tl_cache *c, cudaStream_t stream) {
         take_deltas(c, a, cursor);
         cudaError_t e = tllm::launch_apply_deltas(a, stream);
         if (e != cudaSuccess) return cuda_fail(c, e, "block-table update launch failed");
+        ++c->launches;
     }
     c->pending.clear();
     return TL_OK;
@@ -269,6 +270,7 @@ int launch_rows(tl_cache *c, const std::vector<int> &row_block, const std::vecto
         }
         cudaError_t e = tllm::launch_append(a, stream);
         if (e != cudaSuccess) return cuda_fail(c, e, "append launch failed");
+        ++c->launches;
     }
     // Updates that did not fit in the row launches.
     if (cursor < c->pending.size()) {
@@ -743,6 +745,7 @@ int tl_get_pool_stats(const tl_cache *c, tl_pool_stats *st) {
     st->block_bytes = c->block_bytes;
     st->active_sequences = (int)c->seqs.size();
     st->max_blocks_per_seq = c->max_blocks_per_seq;
+    st->kernel_launches = c->launches;
     return TL_OK;
 }
 
@@ -811,7 +814,7 @@ int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const in
             const Sequence *s = ss[(size_t)(j0 + i)];
             a.slot[i] = s->slot;
             a.len[i] = s->written;
-            a.prefix[i + 1] = a.prefix[i] + ceil_div(s->written, c->bs);
+            a.prefix[i + 1] = a.prefix[i] + ceil_div(s->written, tllm::kDecodeTile);
             if (s->written == 0) {
                 cudaError_t e = cudaMemsetAsync(static_cast<uint16_t *>(a.o) + (long long)i * row, 0,
                                                 (size_t)row * 2, stream);
@@ -823,9 +826,11 @@ int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const in
         a.workers = (int)std::min<long long>(c->max_workers, a.total_items);
         cudaError_t e = tllm::launch_decode(a, c->tmap, stream);
         if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: decode launch failed");
+        ++c->launches;
         if (a.workers > 1) {
             e = tllm::launch_merge(a, stream);
             if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: merge launch failed");
+            ++c->launches;
         }
     }
     return TL_OK;

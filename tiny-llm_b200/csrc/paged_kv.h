@@ -85,6 +85,7 @@ struct tl_cache {
     std::unordered_map<int, tllm::Sequence> seqs;
     std::vector<tllm::BlockDelta> pending;
     int next_seq_id = 0;
+    long long launches = 0;  // kernels launched by this handle
     std::string last_error;
 
     tllm::PoolGeom geom() const;

@@ -84,7 +84,7 @@ class PoolStats(C.Structure):
         ("num_blocks", C.c_longlong), ("used_blocks", C.c_longlong),
         ("free_blocks", C.c_longlong), ("high_water", C.c_longlong),
         ("block_bytes", C.c_longlong), ("active_sequences", C.c_int),
-        ("max_blocks_per_seq", C.c_int),
+        ("max_blocks_per_seq", C.c_int), ("kernel_launches", C.c_longlong),
     ]
 
 
