@@ -48,6 +48,10 @@ CONFIGS = {
                lens=[17, 64, 100, 128], rope=False),
     "c2": dict(workload="c2 Llama-2-7B MHA decode, 32 seqs @ ctx 2048", L=32, Hq=32, Hkv=32,
                D=128, bs=16, lens=[2048] * 32, rope=True),
+    # Profiling case: every decode launch is identical to c2's (32 seqs x 32
+    # heads x 2049 tokens, 1.07 GB of KV), with 2 layers so ~2 GB sits on the GPU.
+    "c2l2": dict(workload="c2 per-launch shape, 2 layers (ncu case)", L=2, Hq=32, Hkv=32,
+                 D=128, bs=16, lens=[2048] * 32, rope=True),
     "c3": dict(workload="c3 Llama-3-8B GQA ragged, 64 seqs ctx U[512,8192], permuted blocks",
                L=32, Hq=32, Hkv=8, D=128, bs=16, lens="ragged", B=64, lo=512, hi=8192,
                rope=True, permute=True),
