@@ -175,6 +175,40 @@ int tl_get_pool(const tl_cache *cache, void **base, size_t *elements);
 int tl_decode_attention(tl_cache *cache, int layer, const void *q, void *o, const int *seq_ids,
                         int num_seqs, float scale, tl_stream_t stream);
 
+/* A paged KV pool that lives in memory the caller owns, laid out as the
+ * handle's pool: fp16 [num_layers][2 (K,V)][num_blocks][block], each block
+ * [block_size][Hkv][D] (token-major) or [Hkv][block_size][D] (head-major);
+ * block_tables is int32 [rows][bt_stride] on the device, entry j of a row
+ * being the block that holds tokens j*block_size .. j*block_size+bs-1. */
+typedef struct {
+    void *pool;
+    const int *block_tables;
+    int *error_word;      /* optional device int: kernels OR error bits into it */
+    long long num_blocks;
+    int num_layers, num_kv_heads, num_q_heads, head_dim, block_size, layout, bt_stride;
+} tl_paged_view;
+
+/* Decode attention that allocates nothing. No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc when they decode — an
+ * engine whose device memory all comes from its own arena or caching
+ * allocator, or a path that must not risk the implicit device
+ * synchronisation of cudaMalloc/cudaFree. Everything is the caller's:
+ * the pool and block tables (`view`), q/o ([num_seqs][Hq][D] fp16, device),
+ * and, on the host, table_rows[i] (the block-table row of sequence i) and
+ * seq_lens[i] (tokens it attends). The math and output are those of
+ * tl_decode_attention. The split-K scratch is a file-scope device array of
+ * 8 MiB inside this library, present on every GPU that loads it until the
+ * process exits; num_seqs above 256, or a shape whose split partials cannot
+ * fit it, are rejected with an error. All calls share that array: calls that
+ * overlap on the GPU race, so order them on one stream. The first call on
+ * each device does a one-time set-up (looks up the array's address, sets
+ * the kernel's shared-memory limit); make it before any stream capture.
+ * On error, a message is copied into error_message (if non-NULL). */
+int tl_decode_attention_static(const tl_paged_view *view, int layer, const void *q, void *o,
+                               const int *table_rows, const int *seq_lens, int num_seqs,
+                               float scale, tl_stream_t stream, char *error_message,
+                               int error_message_size);
+
 /* Synchronizes `stream`, then reads and clears the handle's device error
  * word; returns TL_ERR_DEVICE_FAULT (with a message) if a kernel recorded
  * an out-of-range block/position or a wait that gave up. */

@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = [
     "tl_active_sequence_count", "tl_get_config", "tl_get_block_table", "tl_get_pool_stats",
     "tl_get_pool", "tl_decode_attention", "tl_sync_check", "tl_rope_table",
     "tl_permute_free_blocks", "tl_debug_inject_alloc_failure", "tl_version",
+    "tl_decode_attention_static",
 ]
 
 
@@ -76,6 +77,16 @@ class Config(C.Structure):
         ("num_blocks", C.c_longlong), ("num_q_heads", C.c_int), ("rope_theta", C.c_float),
         ("rope_on_append", C.c_int), ("layout", C.c_int), ("backend", C.c_int),
         ("device", C.c_int),
+    ]
+
+
+class PagedView(C.Structure):
+    """tl_paged_view: a caller-owned pool for tl_decode_attention_static."""
+    _fields_ = [
+        ("pool", C.c_void_p), ("block_tables", C.c_void_p), ("error_word", C.c_void_p),
+        ("num_blocks", C.c_longlong), ("num_layers", C.c_int), ("num_kv_heads", C.c_int),
+        ("num_q_heads", C.c_int), ("head_dim", C.c_int), ("block_size", C.c_int),
+        ("layout", C.c_int), ("bt_stride", C.c_int),
     ]
 
 
@@ -133,6 +144,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_permute_free_blocks": (i, [vp, C.c_ulonglong]),
         "tl_debug_inject_alloc_failure": (i, [i]),
         "tl_version": (C.c_char_p, []),
+        "tl_decode_attention_static": (i, [C.POINTER(PagedView), i, vp, vp, ip, ip, i, f, vp,
+                                           C.c_char_p, i]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -289,6 +302,19 @@ def rope_table(max_pos: int, head_dim: int, theta: float):
     fp = C.POINTER(C.c_float)
     lib.tl_rope_table(cos.ctypes.data_as(fp), sin.ctypes.data_as(fp), max_pos, head_dim, theta)
     return cos, sin
+
+
+def decode_attention_static(view: PagedView, layer, q_ptr, o_ptr, table_rows, seq_lens,
+                            scale=0.0, stream=0):
+    """tl_decode_attention_static: decode over a caller-owned pool, with the
+    library's file-scope split scratch (no allocation by the call)."""
+    lib = load()
+    buf = C.create_string_buffer(512)
+    st = lib.tl_decode_attention_static(C.byref(view), int(layer), q_ptr, o_ptr, _ids(table_rows),
+                                        _ids(seq_lens), len(seq_lens), float(scale),
+                                        stream or None, buf, 512)
+    if st != TL_OK:
+        raise _ERRORS.get(st, TLError)(st, buf.value.decode())
 
 
 def inject_alloc_failure(nth: int) -> None:
