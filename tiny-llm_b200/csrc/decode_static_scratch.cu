@@ -133,7 +133,7 @@ extern "C" int tl_decode_attention_static(const tl_paged_view *view, int layer, 
                                          cudaGetErrorString(e)));
 
     const int G = Hq / Hkv;
-    const size_t per_worker = 2ull * G * (size_t)(D + 2) * sizeof(float);
+    const size_t per_worker = 2ull * G * (size_t)tllm::partial_row_floats(D) * sizeof(float);
     const long long cap_workers = (long long)((kStaticScratchBytes - kErrorSlotBytes) / per_worker);
 
     tllm::DecodeArgs a{};

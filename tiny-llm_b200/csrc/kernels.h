@@ -76,7 +76,9 @@ struct DecodeArgs {
     PoolGeom g;
     const void *q;          // fp16 [nseq][Hq][D]
     void *o;                // fp16 [nseq][Hq][D]
-    float *partial;         // [V][2][G][D+2] fp32 split partials
+    float *partial;         // [V][2][G][D+4] fp32 split partials (acc[D], m, l, pad)
+    int *counters;          // [nseq][Hkv] zeroed tickets: the last worker of a cut
+                            // unit merges it in-kernel; nullptr -> launch_merge pass
     int layer;
     int group;              // G = Hq / Hkv
     float scale_log2;       // softmax scale * log2(e)
@@ -89,6 +91,7 @@ struct DecodeArgs {
 };
 
 // Sizes the kernels need from the host.
+inline int partial_row_floats(int head_dim) { return head_dim + 4; }
 int decode_workers_per_cta();
 int decode_max_workers(int device, int head_dim, int block_size);
 

@@ -61,6 +61,11 @@ struct Cfg {
     static constexpr int kKS = D / 16;                    // k-steps of the QK mma
 };
 
+// Floats per (worker, slot, head) partial row: acc[D], m, l, 2 pad, so rows
+// start on 16-byte boundaries for the float4 reads of the merge.
+template <int D>
+constexpr int kPartialRow = D + 4;
+
 struct ItemPos {
     int b, kvh, tile, nb;
     long long unit_first;
@@ -88,6 +93,96 @@ __device__ __forceinline__ ItemPos locate(const DecodeArgs &a, long long w) {
 
 __device__ __forceinline__ long long worker_start(long long v, long long W, long long V) {
     return v * W / V;
+}
+
+// Combines the partials of one cut unit (sequence b, kv head kvh) left by
+// workers v_first..v_last and writes its fp16 output; one warp. A source
+// stored the unit in slot 0 when the unit was its first piece (its range
+// starts inside the unit), otherwise in slot 1. Lanes split the G heads
+// (32/G' lanes per head, G' = G rounded up to a power of two) and each lane
+// owns float4 chunks of D; sources are folded in with an online softmax
+// merge, two per round with all their loads issued together, so the chain
+// of L2 round trips is ~(number of sources)/2 long.
+template <int D>
+__device__ __forceinline__ void merge_unit(const DecodeArgs &a, long long unit_first, int b,
+                                           int kvh, long long v_first, long long v_last,
+                                           int lane) {
+    constexpr int kRow = kPartialRow<D>;
+    constexpr int kMaxChunks = D / 16;          // float4 chunks per lane at G' = 8
+    constexpr int kPerRound = D <= 128 ? 2 : 1;  // sources per round (register budget)
+    const long long W = a.total_items, V = a.workers;
+    const int G = a.group, H = a.g.num_kv_heads, Hq = H * G;
+    const int gp = G <= 1 ? 1 : (G <= 2 ? 2 : (G <= 4 ? 4 : 8));
+    const int lpg = 32 / gp;                     // lanes per head
+    const int g = lane / lpg, sub = lane % lpg;
+    const int nchunks = (D / 4 + lpg - 1) / lpg;
+    if (g >= G) return;
+    float M = -INFINITY, L = 0.f;
+    float4 O[kMaxChunks];
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long long v = v_first; v <= v_last; v += kPerRound) {
+        float mv[kPerRound], lv[kPerRound];
+        float4 xv[kPerRound][kMaxChunks];
+#pragma unroll
+        for (int r = 0; r < kPerRound; ++r) {
+            const long long u = v + r;
+            mv[r] = -INFINITY;
+            lv[r] = 0.f;
+            if (u <= v_last) {
+                const int slot = worker_start(u, W, V) >= unit_first ? 0 : 1;
+                const float *pb = a.partial + ((u * 2 + slot) * G + g) * (long long)kRow;
+                mv[r] = __ldcg(pb + D);
+                lv[r] = __ldcg(pb + D + 1);
+#pragma unroll
+                for (int k = 0; k < kMaxChunks; ++k) {
+                    const int c = sub + k * lpg;
+                    if (k < nchunks && c < D / 4) xv[r][k] = __ldcg(reinterpret_cast<const float4 *>(pb) + c);
+                }
+            }
+        }
+        float Mn = M;
+#pragma unroll
+        for (int r = 0; r < kPerRound; ++r) Mn = fmaxf(Mn, mv[r]);
+        const float sc = ptx::ex2(M - Mn);
+        float w[kPerRound];
+#pragma unroll
+        for (int r = 0; r < kPerRound; ++r) w[r] = (v + r <= v_last) ? ptx::ex2(mv[r] - Mn) : 0.f;
+        L = L * sc;
+#pragma unroll
+        for (int r = 0; r < kPerRound; ++r) L += w[r] * lv[r];
+#pragma unroll
+        for (int k = 0; k < kMaxChunks; ++k) {
+            if (k < nchunks) {
+                float4 o = O[k];
+                o.x *= sc; o.y *= sc; o.z *= sc; o.w *= sc;
+#pragma unroll
+                for (int r = 0; r < kPerRound; ++r) {
+                    if (v + r <= v_last) {
+                        o.x += w[r] * xv[r][k].x; o.y += w[r] * xv[r][k].y;
+                        o.z += w[r] * xv[r][k].z; o.w += w[r] * xv[r][k].w;
+                    }
+                }
+                O[k] = o;
+            }
+        }
+        M = Mn;
+    }
+    const float inv = 1.f / L;
+    __half *o = static_cast<__half *>(a.o) + ((long long)b * Hq + (long long)kvh * G + g) * D;
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+        const int c = sub + k * lpg;
+        if (k < nchunks && c < D / 4) {
+            // two 4-byte stores: the API only promises 4-byte aligned outputs
+            *reinterpret_cast<__half2 *>(o + 4 * c) = __floats2half2_rn(O[k].x * inv, O[k].y * inv);
+            *reinterpret_cast<__half2 *>(o + 4 * c + 2) = __floats2half2_rn(O[k].z * inv, O[k].w * inv);
+        }
+    }
+}
+
+__device__ __forceinline__ long long worker_of_item(long long x, long long W, long long V) {
+    return ((x + 1) * V + W - 1) / W - 1;  // largest v with worker_start(v) <= x
 }
 
 template <int D>
@@ -120,6 +215,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         ptx::fence_barrier_init();
     }
     __syncwarp();
+    // Programmatic dependent launch: the next kernel in the stream may begin
+    // launching now (its CTAs only fit as ours retire); this kernel reads
+    // nothing from global memory before the previous grid has completed.
+    ptx::griddep_launch_dependents();
+    ptx::griddep_wait();
 
     const uint64_t policy = ptx::l2_policy_evict_first();
     const long long layer_k_row = (long long)(a.layer * 2 + 0) * g.num_blocks;
@@ -224,27 +324,44 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
             }
         } else {
             const int slot = first_piece ? 0 : 1;
-            float *pbase = a.partial + ((worker * 2 + slot) * G) * (long long)(D + 2);
+            float *pbase = a.partial + ((worker * 2 + slot) * G) * (long long)kPartialRow<D>;
 #pragma unroll
             for (int dm = 0; dm < C::kKS; ++dm) {
                 const int d = dm * 16 + gid;
                 if (g0 < G) {
-                    pbase[g0 * (D + 2) + d] = acc[dm][0];
-                    pbase[g0 * (D + 2) + d + 8] = acc[dm][2];
+                    pbase[g0 * kPartialRow<D> + d] = acc[dm][0];
+                    pbase[g0 * kPartialRow<D> + d + 8] = acc[dm][2];
                 }
                 if (g1 < G) {
-                    pbase[g1 * (D + 2) + d] = acc[dm][1];
-                    pbase[g1 * (D + 2) + d + 8] = acc[dm][3];
+                    pbase[g1 * kPartialRow<D> + d] = acc[dm][1];
+                    pbase[g1 * kPartialRow<D> + d + 8] = acc[dm][3];
                 }
             }
             if (gid == 0) {
                 if (g0 < G) {
-                    pbase[g0 * (D + 2) + D] = m0;
-                    pbase[g0 * (D + 2) + D + 1] = lt0;
+                    pbase[g0 * kPartialRow<D> + D] = m0;
+                    pbase[g0 * kPartialRow<D> + D + 1] = lt0;
                 }
                 if (g1 < G) {
-                    pbase[g1 * (D + 2) + D] = m1;
-                    pbase[g1 * (D + 2) + D + 1] = lt1;
+                    pbase[g1 * kPartialRow<D> + D] = m1;
+                    pbase[g1 * kPartialRow<D> + D + 1] = lt1;
+                }
+            }
+            if (a.counters) {
+                // The last worker to finish a piece of this unit merges it:
+                // an atomic ticket, no waiting on other workers.
+                __threadfence();
+                __syncwarp();
+                const long long v_first = worker_of_item(ufirst, W, V);
+                const long long v_last = worker_of_item(ufirst + unb - 1, W, V);
+                int *ctr = a.counters + ((long long)ub * H + ukvh);
+                int last = 0;
+                if (lane == 0) last = atomicAdd(ctr, 1) == (int)(v_last - v_first);
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    merge_unit<D>(a, ufirst, ub, ukvh, v_first, v_last, lane);
+                    if (lane == 0) *ctr = 0;  // ready for the next launch
                 }
             }
         }
@@ -407,13 +524,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     if (ub >= 0) finalize();
 }
 
-// Combines the partials of every unit that was cut by a worker boundary.
-// CTA v merges the unit that contains worker v's first item when that unit
-// started in an earlier worker and ends inside worker v (so each cut unit
-// has exactly one merger). Sources are workers v_first..v; a source whose
-// first item lies inside the unit stored it in slot 0, otherwise slot 1.
+// Second pass for launches without merge counters: CTA v merges the unit
+// that contains worker v's first item when that unit started in an earlier
+// worker and ends inside v, so each cut unit has exactly one merger.
 template <int D>
-__global__ void __launch_bounds__(128) merge_kernel(const __grid_constant__ DecodeArgs a) {
+__global__ void __launch_bounds__(32) merge_kernel(const __grid_constant__ DecodeArgs a) {
     const long long v = blockIdx.x;
     const long long W = a.total_items, V = a.workers;
     const long long ws = worker_start(v, W, V), we = worker_start(v + 1, W, V);
@@ -421,27 +536,7 @@ __global__ void __launch_bounds__(128) merge_kernel(const __grid_constant__ Deco
     const ItemPos p = locate(a, ws);
     const long long ulast = p.unit_first + p.nb - 1;
     if (p.unit_first >= ws || ulast >= we) return;
-    const long long v_first = ((p.unit_first + 1) * V + W - 1) / W - 1;
-    const int G = a.group, H = a.g.num_kv_heads, Hq = H * G;
-    __half *o = static_cast<__half *>(a.o) + ((long long)p.b * Hq + (long long)p.kvh * G) * D;
-    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-        const int gg = idx / D, d = idx % D;
-        float M = -INFINITY;
-        for (long long u = v_first; u <= v; ++u) {
-            const int slot = worker_start(u, W, V) >= p.unit_first ? 0 : 1;
-            const float *pb = a.partial + ((u * 2 + slot) * G + gg) * (long long)(D + 2);
-            M = fmaxf(M, pb[D]);
-        }
-        float L = 0.f, O = 0.f;
-        for (long long u = v_first; u <= v; ++u) {
-            const int slot = worker_start(u, W, V) >= p.unit_first ? 0 : 1;
-            const float *pb = a.partial + ((u * 2 + slot) * G + gg) * (long long)(D + 2);
-            const float f = ptx::ex2(pb[D] - M);
-            L += f * pb[D + 1];
-            O += f * pb[d];
-        }
-        o[(long long)gg * D + d] = __float2half_rn(O / L);
-    }
+    merge_unit<D>(a, p.unit_first, p.b, p.kvh, worker_of_item(p.unit_first, W, V), v, threadIdx.x);
 }
 
 // Opts the kernel into its dynamic shared memory size, once per device.
@@ -463,10 +558,17 @@ template <int D>
 cudaError_t launch_decode_t(const DecodeArgs &a, const void *tmap128, cudaStream_t s) {
     cudaError_t e = prepare<D>();
     if (e != cudaSuccess) return e;
-    const int ctas = (a.workers + kWarps - 1) / kWarps;
-    paged_decode_kernel<D><<<ctas, kWarps * 32, Cfg<D>::kSmemBytes, s>>>(
-        *static_cast<const CUtensorMap *>(tmap128), a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.workers + kWarps - 1) / kWarps);
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = Cfg<D>::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, paged_decode_kernel<D>, *static_cast<const CUtensorMap *>(tmap128), a);
 }
 
 template <int D>
@@ -505,9 +607,9 @@ cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t
 
 cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s) {
     switch (a.g.head_dim) {
-    case 64: merge_kernel<64><<<a.workers, 128, 0, s>>>(a); break;
-    case 128: merge_kernel<128><<<a.workers, 128, 0, s>>>(a); break;
-    case 256: merge_kernel<256><<<a.workers, 128, 0, s>>>(a); break;
+    case 64: merge_kernel<64><<<a.workers, 32, 0, s>>>(a); break;
+    case 128: merge_kernel<128><<<a.workers, 32, 0, s>>>(a); break;
+    case 256: merge_kernel<256><<<a.workers, 32, 0, s>>>(a); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -482,10 +482,13 @@ int tl_create(const tl_config *cfg_in, tl_cache **out) {
         c->max_workers = tllm::decode_max_workers(c->device, cfg.head_dim, bs);
         if (c->max_workers <= 0) return fail(TL_ERR_CUDA, "KVCacheManager: decode kernel occupancy query failed");
         c->partial_floats =
-            (size_t)c->max_workers * 2 * (size_t)c->group * (size_t)(cfg.head_dim + 2);
+            (size_t)c->max_workers * 2 * (size_t)c->group * (size_t)tllm::partial_row_floats(cfg.head_dim);
         if (storage_alloc(c, &p, c->partial_floats * 4, &why))
             return fail(TL_ERR_CUDA, "KVCacheManager: split scratch allocation failed: " + why);
         c->partial = static_cast<float *>(p);
+        if (storage_alloc(c, &p, (size_t)tllm::kMaxDecodeSeqs * cfg.num_kv_heads * sizeof(int), &why))
+            return fail(TL_ERR_CUDA, "KVCacheManager: merge counter allocation failed: " + why);
+        c->merge_counters = static_cast<int *>(p);
         cudaError_t e = tllm::encode_pool_tensor_map(c->geom(), c->tmap);
         if (e != cudaSuccess)
             return fail(TL_ERR_CUDA, std::string("KVCacheManager: tensor map encode failed: ") +
@@ -510,6 +513,7 @@ void tl_destroy(tl_cache *c) {
         storage_free(c, c->rope_cos);
         storage_free(c, c->rope_sin);
         storage_free(c, c->partial);
+        storage_free(c, c->merge_counters);
     }
     delete c;
 }
@@ -805,6 +809,7 @@ int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const in
         a.q = static_cast<const uint16_t *>(q) + j0 * row;
         a.o = static_cast<uint16_t *>(o) + j0 * row;
         a.partial = c->partial;
+        a.counters = c->merge_counters;  // in-kernel merge of cut units
         a.layer = layer;
         a.group = c->group;
         a.scale_log2 = scale * 1.4426950408889634f;
@@ -827,11 +832,6 @@ int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const in
         cudaError_t e = tllm::launch_decode(a, c->tmap, stream);
         if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: decode launch failed");
         ++c->launches;
-        if (a.workers > 1) {
-            e = tllm::launch_merge(a, stream);
-            if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: merge launch failed");
-            ++c->launches;
-        }
     }
     return TL_OK;
 }
@@ -847,6 +847,10 @@ int tl_sync_check(tl_cache *c, tl_stream_t stream) {
     if (e != cudaSuccess) return cuda_fail(c, e, "sync: error-word read failed");
     if (word != 0) {
         cudaMemset(c->err_word, 0, sizeof(int));
+        // A worker that stopped early may have left merge tickets behind.
+        if (c->merge_counters)
+            cudaMemset(c->merge_counters, 0,
+                       (size_t)tllm::kMaxDecodeSeqs * c->cfg.num_kv_heads * sizeof(int));
         std::string m = "device error word 0x" + [&] {
             char buf[16];
             std::snprintf(buf, sizeof buf, "%x", word);

@@ -76,6 +76,7 @@ struct tl_cache {
     float *rope_cos = nullptr;
     float *rope_sin = nullptr;
     float *partial = nullptr;
+    int *merge_counters = nullptr;  // [kMaxDecodeSeqs][Hkv], zero between launches
     size_t partial_floats = 0;
     int max_workers = 0;
     alignas(64) unsigned char tmap[128];
