@@ -172,8 +172,19 @@ def run_ours(cfg, args, world, rank, local):
     import torch
     import tiny_llm_b200 as T
 
+    from tiny_llm_b200 import dist as TD
+
     L, Hq, Hkv, D, bs = cfg["L"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["bs"]
-    lens = seq_lens(cfg, args.seed, rank)
+    head = args.shard == "head"
+    if head:
+        # every rank holds all sequences but only its slice of the KV heads
+        # (and the query heads reading them); outputs are all-gathered
+        sl = TD.head_shard(Hkv, Hq, world, rank)
+        Hkv, Hq = sl.kv_count, sl.q_count
+        lens = seq_lens(cfg, args.seed, 0)
+    else:
+        lens = seq_lens(cfg, args.seed, rank)
+    kcfg = dict(cfg, Hkv=Hkv, Hq=Hq)
     B = len(lens)
     steps = args.warmup + args.steps
     e2e_steps = args.warmup + args.steps
@@ -204,8 +215,13 @@ def run_ours(cfg, args, world, rank, local):
     vnew = [torch.randn((L, B, Hkv, D), dtype=torch.float16, device="cuda", generator=gen) for _ in range(nbuf)]
     q = [torch.randn((L, B, Hq, D), dtype=torch.float16, device="cuda", generator=gen) for _ in range(nbuf)]
     out = [torch.empty((L, B, Hq, D), dtype=torch.float16, device="cuda") for _ in range(nbuf)]
+    gathered = torch.empty((L, world, B, Hq, D), dtype=torch.float16, device="cuda") if head else None
     scale = 1.0 / math.sqrt(D)
     cur = list(lens)
+
+    def after_decode(b, l):
+        if head and world > 1:  # the layer's outputs, all heads, on every rank
+            TD.gather_head_outputs(out[b][l], gathered[l])
 
     dec_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(L * args.steps)]
@@ -233,12 +249,13 @@ def run_ours(cfg, args, world, rank, local):
             cache.decode_attention(l, q[b][l].data_ptr(), out[b][l].data_ptr(), sids, scale, sp)
             if timed:
                 dec_ev[(i - args.warmup) * L + l][1].record(stream)
+            after_decode(b, l)
         for s in sids:
             cache.advance_seq_len(s, 1)
         cur = attended
         if timed:
-            kv_total += kv_bytes(attended, cfg)
-            dec_bytes += kv_bytes(attended, cfg) + 2 * L * B * Hq * D * 2 + \
+            kv_total += kv_bytes(attended, kcfg)
+            dec_bytes += kv_bytes(attended, kcfg) + 2 * L * B * Hq * D * 2 + \
                 sum(-(-s // bs) for s in attended) * 4 * L
     end.record(stream)
     end.synchronize()
@@ -283,6 +300,7 @@ def run_ours(cfg, args, world, rank, local):
             attended = [c + 1 for c in cur]
             for l in range(L):
                 cache.decode_attention(l, q[b][l].data_ptr(), out[b][l].data_ptr(), sids, scale, sp)
+                after_decode(b, l)
             comp_done[b].record(stream)
             for s in sids:
                 cache.advance_seq_len(s, 1)
@@ -293,7 +311,7 @@ def run_ours(cfg, args, world, rank, local):
                 copy.wait_event(comp_done[b])
                 ho[b].copy_(out[b], non_blocking=True)
             if account:
-                kvb += kv_bytes(attended, cfg)
+                kvb += kv_bytes(attended, kcfg)
         return kvb
 
     e2e_loop(args.warmup, False)
@@ -496,6 +514,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--layout", choices=["token", "head"], default="token")
+    ap.add_argument("--shard", choices=["batch", "head"], default="batch",
+                    help="multi-GPU split: whole sequences per rank (weak scaling) or KV heads "
+                         "per rank with an all-gather of outputs each layer (strong scaling)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -507,7 +528,9 @@ def main():
     base_config = {"workload": cfg["workload"], "layers": cfg["L"], "q_heads": cfg["Hq"],
                    "kv_heads": cfg["Hkv"], "head_dim": cfg["D"], "block_size": cfg["bs"],
                    "rope_on_append": cfg["rope"], "layout": args.layout,
-                   "parallelism": f"batch-shard x{world} (independent sequences per GPU)",
+                   "parallelism": (f"head-shard x{world} (KV heads per GPU, NCCL all-gather of outputs per layer)"
+                                   if args.shard == "head" else
+                                   f"batch-shard x{world} (independent sequences per GPU)"),
                    "l2": "KV bytes per step far above the 126 MB L2; no flush needed",
                    "seed": args.seed}
 
@@ -516,6 +539,9 @@ def main():
         if res is None:
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
             return
         ms = barrier_max(res["ms"], world)
         kv = barrier_sum(res["kv"], world)
@@ -540,6 +566,9 @@ def main():
                     "decode_kernel_gbs": round(kv / world / (res["dec_ms"] / 1e3) / 1e9, 1) if res["dec_ms"] else None,
                     "clocks": res["clocks"]}
             print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
         return
 
     res = run_ours(cfg, args, world, rank, local)
@@ -563,10 +592,11 @@ def main():
                 "ms_per_step": round(ms / args.steps, 4),
                 "us_per_step": round(1e3 * ms / args.steps, 1),
                 "pct_hbm_peak_per_gpu": round(100 * value / world / peak, 1),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f16 (fp32 accumulate)",
+                "higher_is_better": True, "scaling": "strong" if args.shard == "head" else "weak",
+                "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
                 "data": "synthetic N(0,1) fp16 K/V/Q from a seeded generator (no dataset)",
-                "config": dict(base_config, global_batch=res["B"] * world, seq_len=max(res["lens"])),
+                "config": dict(base_config, global_batch=res["B"] * (1 if args.shard == "head" else world),
+                               seq_len=max(res["lens"])),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                              "unit": "GB/s", "frac": round(achieved / peak, 4),
                              "traffic": traffic, "kernel": "paged_decode_kernel + merge_kernel",

@@ -1,0 +1,109 @@
+"""Head-sharded decode on 2 GPUs (one process per GPU, NCCL): each rank
+appends and decodes only its KV heads through the C-ABI, the per-layer
+outputs are all-gathered, and every rank's reassembled [B][Hq][D] must match
+the fp64 oracle of the full model within the attention tolerance. Skipped
+with fewer than 2 GPUs. NVLS is off, as for every multi-GPU test here."""
+import math
+import multiprocessing as mp
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import conftest
+
+ROOT = Path(__file__).resolve().parents[1]
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, q_out):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    sys.path.insert(0, str(ROOT / "tiny-llm_b200" / "python"))
+    sys.path.insert(0, str(ROOT / "oracle"))
+    sys.path.insert(0, str(ROOT / "tests"))
+    try:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        import oracle as O
+        import tiny_llm_b200 as T
+        from tiny_llm_b200 import dist as TD
+        from gpu_helpers import check_close, from_dev, to_dev
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        L, Hq, Hkv, D, bs = 2, 16, 2, 128, 32
+        lens = [700, 33, 1500]
+        sl = TD.head_shard(Hkv, Hq, world, rank)
+        cache = T.KVCache(num_layers=L, num_kv_heads=sl.kv_count, head_dim=D, max_seq_len=2048,
+                          max_batch_size=len(lens), block_size=bs, num_q_heads=sl.q_count,
+                          rope_on_append=True, device=rank)
+        cos, sin = O.rope_table(2048, D, 10000.0)
+        full_k, full_v = {}, {}
+        sids = []
+        keep = []
+        for i, S in enumerate(lens):
+            sid = cache.allocate_sequence(2048)
+            sids.append(sid)
+            for l in range(L):
+                k = O.normal_f16((S, Hkv, D), 1000 * i + 2 * l)
+                v = O.normal_f16((S, Hkv, D), 1000 * i + 2 * l + 1)
+                full_k[(i, l)] = np.stack([O.rope_row(k[t], cos, sin, t) for t in range(S)])
+                full_v[(i, l)] = v
+                ks = to_dev(np.ascontiguousarray(k[:, sl.kv_first: sl.kv_first + sl.kv_count]))
+                vs = to_dev(np.ascontiguousarray(v[:, sl.kv_first: sl.kv_first + sl.kv_count]))
+                keep += [ks, vs]
+                cache.append_kv(sid, l, ks.data_ptr(), vs.data_ptr(), S)
+            cache.advance_seq_len(sid, S)
+        scale = 1.0 / math.sqrt(D)
+        ok = True
+        for l in range(L):
+            q = O.normal_f16((len(lens), Hq, D), 77 + l)
+            qs = to_dev(np.ascontiguousarray(q[:, sl.q_first: sl.q_first + sl.q_count]))
+            o = torch.empty((len(lens), sl.q_count, D), dtype=torch.float16, device="cuda")
+            cache.decode_attention(l, qs.data_ptr(), o.data_ptr(), sids, scale)
+            gathered = torch.empty((world, len(lens), sl.q_count, D), dtype=torch.float16, device="cuda")
+            TD.gather_head_outputs(o, gathered)
+            full = TD.rank_major_to_heads(gathered)
+            cache.sync_check()
+            got = O.f16_to_f32(from_dev(full))
+            for i in range(len(lens)):
+                ref = O.decode_one(q[i], full_k[(i, l)], full_v[(i, l)], scale)
+                check_close(got[i], ref, f"rank {rank} layer {l} seq {i}")
+        cache.close()
+        dist.destroy_process_group()
+        q_out.put((rank, "ok"))
+    except Exception as e:
+        q_out.put((rank, "fail: " + repr(e)))
+
+
+def test_head_sharded_decode_two_gpus():
+    if not conftest.cuda_available():
+        pytest.skip("no CUDA device")
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert res == {0: "ok", 1: "ok"}, res

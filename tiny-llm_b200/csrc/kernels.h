@@ -22,6 +22,8 @@ constexpr int kMaxDeltas = 96;
 constexpr int kMaxDecodeSeqs = 256;
 // Decode work item: 16 tokens of one KV head (a block of 32 is two items).
 constexpr int kDecodeTile = 16;
+// Units cut into more pieces than this are merged by the wide merge pass.
+constexpr int kInKernelMergeMaxPieces = 12;
 
 // Pool geometry shared by every kernel.
 struct PoolGeom {

@@ -524,19 +524,74 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     if (ub >= 0) finalize();
 }
 
-// Second pass for launches without merge counters: CTA v merges the unit
-// that contains worker v's first item when that unit started in an earlier
-// worker and ends inside v, so each cut unit has exactly one merger.
+// Second pass for launches without merge counters (and for units cut into
+// many pieces, where one warp would have to read hundreds of KB of
+// partials). One CTA per (unit, head): blockIdx.x = sequence*Hkv + kv_head,
+// blockIdx.y = head g of the group. Its 1024 threads are D/4 chunk lanes x
+// (4096/D) source groups; each group folds every kGroups-th source with an
+// online softmax merge (independent loads), then the groups are combined in
+// shared memory. Complete units (one worker) were written by the decode
+// kernel and are skipped. Launched as a programmatic dependent of the decode
+// kernel: it waits for the decode grid before reading any partial.
 template <int D>
-__global__ void __launch_bounds__(32) merge_kernel(const __grid_constant__ DecodeArgs a) {
-    const long long v = blockIdx.x;
+__global__ void __launch_bounds__(1024) merge_kernel(const __grid_constant__ DecodeArgs a) {
+    constexpr int kRow = kPartialRow<D>;
+    constexpr int kChunks = D / 4;
+    constexpr int kGroups = 1024 / kChunks;
+    __shared__ float s_m[kGroups][kChunks];
+    __shared__ float s_l[kGroups][kChunks];
+    __shared__ float4 s_o[kGroups][kChunks];
+    ptx::griddep_launch_dependents();
+    ptx::griddep_wait();
+    const int H = a.g.num_kv_heads, G = a.group, Hq = H * G;
+    const int b = blockIdx.x / H, kvh = blockIdx.x % H, g = blockIdx.y;
+    if (b >= a.nseq || g >= G) return;
+    const int nb = a.prefix[b + 1] - a.prefix[b];
+    if (nb == 0) return;
     const long long W = a.total_items, V = a.workers;
-    const long long ws = worker_start(v, W, V), we = worker_start(v + 1, W, V);
-    if (we <= ws) return;
-    const ItemPos p = locate(a, ws);
-    const long long ulast = p.unit_first + p.nb - 1;
-    if (p.unit_first >= ws || ulast >= we) return;
-    merge_unit<D>(a, p.unit_first, p.b, p.kvh, worker_of_item(p.unit_first, W, V), v, threadIdx.x);
+    const long long unit_first = (long long)H * a.prefix[b] + (long long)kvh * nb;
+    const long long v_first = worker_of_item(unit_first, W, V);
+    const long long v_last = worker_of_item(unit_first + nb - 1, W, V);
+    if (v_first == v_last) return;
+    const int c = threadIdx.x % kChunks, sg = threadIdx.x / kChunks;
+    float M = -INFINITY, L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long long u = v_first + sg; u <= v_last; u += kGroups) {
+        const int slot = worker_start(u, W, V) >= unit_first ? 0 : 1;
+        const float *pb = a.partial + ((u * 2 + slot) * G + g) * (long long)kRow;
+        const float m = __ldcg(pb + D), l = __ldcg(pb + D + 1);
+        const float4 x = __ldcg(reinterpret_cast<const float4 *>(pb) + c);
+        const float Mn = fmaxf(M, m);
+        const float sc = ptx::ex2(M - Mn), w = ptx::ex2(m - Mn);
+        L = L * sc + w * l;
+        O.x = O.x * sc + w * x.x;
+        O.y = O.y * sc + w * x.y;
+        O.z = O.z * sc + w * x.z;
+        O.w = O.w * sc + w * x.w;
+        M = Mn;
+    }
+    s_m[sg][c] = M;
+    s_l[sg][c] = L;
+    s_o[sg][c] = O;
+    __syncthreads();
+    if (sg != 0) return;
+    float Mf = -INFINITY;
+    for (int j = 0; j < kGroups; ++j) Mf = fmaxf(Mf, s_m[j][c]);
+    float Lf = 0.f;
+    float4 Of = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < kGroups; ++j) {
+        const float w = ptx::ex2(s_m[j][c] - Mf);  // empty groups: m = -inf -> 0
+        const float4 x = s_o[j][c];
+        Lf += w * s_l[j][c];
+        Of.x += w * x.x;
+        Of.y += w * x.y;
+        Of.z += w * x.z;
+        Of.w += w * x.w;
+    }
+    const float inv = 1.f / Lf;
+    __half *o = static_cast<__half *>(a.o) + ((long long)b * Hq + (long long)kvh * G + g) * D + 4 * c;
+    *reinterpret_cast<__half2 *>(o) = __floats2half2_rn(Of.x * inv, Of.y * inv);
+    *reinterpret_cast<__half2 *>(o + 2) = __floats2half2_rn(Of.z * inv, Of.w * inv);
 }
 
 // Opts the kernel into its dynamic shared memory size, once per device.
@@ -605,14 +660,27 @@ cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t
     }
 }
 
+template <int D>
+cudaError_t launch_merge_t(const DecodeArgs &a, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nseq * a.g.num_kv_heads, a.group);
+    cfg.blockDim = dim3(1024);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, merge_kernel<D>, a);
+}
+
 cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s) {
     switch (a.g.head_dim) {
-    case 64: merge_kernel<64><<<a.workers, 32, 0, s>>>(a); break;
-    case 128: merge_kernel<128><<<a.workers, 32, 0, s>>>(a); break;
-    case 256: merge_kernel<256><<<a.workers, 32, 0, s>>>(a); break;
+    case 64: return launch_merge_t<64>(a, s);
+    case 128: return launch_merge_t<128>(a, s);
+    case 256: return launch_merge_t<256>(a, s);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128) {

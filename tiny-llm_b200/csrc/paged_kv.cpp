@@ -829,9 +829,21 @@ int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const in
         a.total_items = (long long)Hkv * a.prefix[n];
         if (a.total_items == 0) continue;
         a.workers = (int)std::min<long long>(c->max_workers, a.total_items);
+        // Few long units cut into many pieces: merge them in a wide second
+        // pass instead of by one warp inside the decode kernel.
+        int max_tiles = 0;
+        for (int i = 0; i < n; ++i) max_tiles = std::max(max_tiles, a.prefix[i + 1] - a.prefix[i]);
+        const long long pieces = (long long)max_tiles * a.workers / a.total_items + 2;
+        const bool two_pass = pieces > tllm::kInKernelMergeMaxPieces;
+        if (two_pass) a.counters = nullptr;
         cudaError_t e = tllm::launch_decode(a, c->tmap, stream);
         if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: decode launch failed");
         ++c->launches;
+        if (two_pass) {
+            e = tllm::launch_merge(a, stream);
+            if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: merge launch failed");
+            ++c->launches;
+        }
     }
     return TL_OK;
 }
