@@ -215,12 +215,29 @@ def run_ours(cfg, args, world, rank, local):
     vnew = [torch.randn((L, B, Hkv, D), dtype=torch.float16, device="cuda", generator=gen) for _ in range(nbuf)]
     q = [torch.randn((L, B, Hq, D), dtype=torch.float16, device="cuda", generator=gen) for _ in range(nbuf)]
     out = [torch.empty((L, B, Hq, D), dtype=torch.float16, device="cuda") for _ in range(nbuf)]
-    gathered = torch.empty((L, world, B, Hq, D), dtype=torch.float16, device="cuda") if head else None
+    p2p = head and world > 1 and args.gather == "p2p"
+    gathered = torch.empty((L, world, B, Hq, D), dtype=torch.float16, device="cuda") \
+        if head and not p2p else None
+    slice_bytes = B * Hq * D * 2
+    if p2p:  # NVLink peer stores from the decode epilogue + epoch flags
+        TD.connect_peer_gather(cache, L * world * slice_bytes)
+        gptr, _ = cache.peer_buffer()
+        torch.cuda.synchronize()
+        barrier(world)  # ranks enter the GPU-side flag waits together
+    epoch = [0]
     scale = 1.0 / math.sqrt(D)
     cur = list(lens)
 
+    def decode(b, l):
+        if p2p:  # decode + publish + pull of the other ranks' slices, fused
+            epoch[0] += 1
+            cache.decode_attention_peer(l, q[b][l].data_ptr(), sids, l * world * slice_bytes,
+                                        epoch[0], scale, sp)
+        else:
+            cache.decode_attention(l, q[b][l].data_ptr(), out[b][l].data_ptr(), sids, scale, sp)
+
     def after_decode(b, l):
-        if head and world > 1:  # the layer's outputs, all heads, on every rank
+        if head and world > 1 and not p2p:  # the layer's outputs, all heads, on every rank
             TD.gather_head_outputs(out[b][l], gathered[l])
 
     dec_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -235,9 +252,9 @@ def run_ours(cfg, args, world, rank, local):
         timed = i >= args.warmup
         if i == args.warmup:
             torch.cuda.synchronize()
-            barrier(world)
             sampler = ClockSampler(local)
             time.sleep(0.3)
+            barrier(world)  # after the sampler starts: ranks enter the timed steps together
             launches0 = cache.pool_stats().kernel_launches
             start.record(stream)
         b = i % nbuf
@@ -246,7 +263,7 @@ def run_ours(cfg, args, world, rank, local):
         for l in range(L):
             if timed:
                 dec_ev[(i - args.warmup) * L + l][0].record(stream)
-            cache.decode_attention(l, q[b][l].data_ptr(), out[b][l].data_ptr(), sids, scale, sp)
+            decode(b, l)
             if timed:
                 dec_ev[(i - args.warmup) * L + l][1].record(stream)
             after_decode(b, l)
@@ -270,7 +287,10 @@ def run_ours(cfg, args, world, rank, local):
     hk = torch.empty((nbuf, L, B, Hkv, D), dtype=torch.float16, pin_memory=True)
     hv = torch.empty_like(hk)
     hq = torch.empty((nbuf, L, B, Hq, D), dtype=torch.float16, pin_memory=True)
-    ho = torch.empty((nbuf, L, B, Hq, D), dtype=torch.float16, pin_memory=True)
+    oshape = (L, world, B, Hq, D) if head and world > 1 else (L, B, Hq, D)
+    ho = torch.empty((nbuf,) + oshape, dtype=torch.float16, pin_memory=True)
+    rt = C.CDLL("libcudart.so.12")  # the runtime torch loaded (same context)
+    rt.cudaMemcpyAsync.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p]
     hk.copy_(torch.stack(knew).cpu())
     hv.copy_(torch.stack(vnew).cpu())
     hq.copy_(torch.stack(q).cpu())
@@ -299,7 +319,7 @@ def run_ours(cfg, args, world, rank, local):
             cache.append_kv_all_layers(sids, knew[b].data_ptr(), vnew[b].data_ptr(), sp)
             attended = [c + 1 for c in cur]
             for l in range(L):
-                cache.decode_attention(l, q[b][l].data_ptr(), out[b][l].data_ptr(), sids, scale, sp)
+                decode(b, l)
                 after_decode(b, l)
             comp_done[b].record(stream)
             for s in sids:
@@ -309,11 +329,16 @@ def run_ours(cfg, args, world, rank, local):
                 h2d(i + 1)  # the next step's inputs cross PCIe under this step's kernels
             with torch.cuda.stream(copy):
                 copy.wait_event(comp_done[b])
-                ho[b].copy_(out[b], non_blocking=True)
+                if p2p:  # the step's result is the gathered outputs of every layer
+                    rt.cudaMemcpyAsync(ho[b].data_ptr(), gptr, ho[b].numel() * 2, 2, copy.cuda_stream)
+                else:
+                    ho[b].copy_(out[b] if gathered is None else gathered, non_blocking=True)
             if account:
                 kvb += kv_bytes(attended, kcfg)
         return kvb
 
+    torch.cuda.synchronize()
+    barrier(world)
     e2e_loop(args.warmup, False)
     torch.cuda.synchronize()
     barrier(world)
@@ -425,9 +450,9 @@ def run_reference(cfg, args, world, rank, local):
     for i in range(steps):
         if i == args.warmup:
             torch.cuda.synchronize()
-            barrier(world)
             sampler = ClockSampler(local)
             time.sleep(0.3)
+            barrier(world)
             start.record(stream)
         evs = None
         if i >= args.warmup:
@@ -514,6 +539,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--layout", choices=["token", "head"], default="token")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="head-shard output exchange: NVLink peer stores from the decode "
+                         "epilogue, or an NCCL all-gather after each layer")
     ap.add_argument("--shard", choices=["batch", "head"], default="batch",
                     help="multi-GPU split: whole sequences per rank (weak scaling) or KV heads "
                          "per rank with an all-gather of outputs each layer (strong scaling)")
@@ -528,7 +556,9 @@ def main():
     base_config = {"workload": cfg["workload"], "layers": cfg["L"], "q_heads": cfg["Hq"],
                    "kv_heads": cfg["Hkv"], "head_dim": cfg["D"], "block_size": cfg["bs"],
                    "rope_on_append": cfg["rope"], "layout": args.layout,
-                   "parallelism": (f"head-shard x{world} (KV heads per GPU, NCCL all-gather of outputs per layer)"
+                   "parallelism": (f"head-shard x{world} (KV heads per GPU, outputs gathered per layer by "
+                                   + ("NVLink peer stores from the decode epilogue)" if args.gather == "p2p"
+                                      else "NCCL all-gather)")
                                    if args.shard == "head" else
                                    f"batch-shard x{world} (independent sequences per GPU)"),
                    "l2": "KV bytes per step far above the 126 MB L2; no flush needed",

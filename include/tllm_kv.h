@@ -175,6 +175,35 @@ int tl_get_pool(const tl_cache *cache, void **base, size_t *elements);
 int tl_decode_attention(tl_cache *cache, int layer, const void *q, void *o, const int *seq_ids,
                         int num_seqs, float scale, tl_stream_t stream);
 
+/* ---- Head-sharded decode across the GPUs of one node -------------------
+ * No reference counterpart (the reference is single-GPU). With KV heads
+ * split over `world` ranks (one process per GPU), each rank's decode writes
+ * its output slice into its own gather area; the last CTA of the launch
+ * publishes an epoch in this rank's flag (one system-scope release) and then
+ * pulls every other rank's slice over NVLink (CUDA IPC mappings, plain
+ * loads) as soon as that rank's flag shows the epoch. Gather area layout, on
+ * every rank: [world][num_seqs][Hq_local][D] fp16 at out_offset
+ * (rank-major). */
+#define TL_IPC_HANDLE_BYTES 64
+/* Allocates this rank's gather region (gather_bytes of outputs plus flags)
+ * and writes its IPC handle (TL_IPC_HANDLE_BYTES) to ipc_handle, for the
+ * caller to exchange with the other ranks. */
+int tl_peer_init(tl_cache *cache, int rank, int world, size_t gather_bytes, void *ipc_handle);
+/* Opens every other rank's region from ipc_handles ([world][64] bytes). */
+int tl_peer_connect(tl_cache *cache, const void *ipc_handles);
+/* Device address and size of this rank's gathered-output area. */
+int tl_peer_buffer(const tl_cache *cache, void **gathered, size_t *bytes);
+/* tl_decode_attention for this rank's heads, all ranks calling it for the
+ * same layer with the same out_offset, num_seqs and `epoch` (a value that
+ * increases call to call). This rank's [num_seqs][Hq][D] slice lands at
+ * out_offset + rank*slice of its gather area (16-byte aligned offset, at
+ * most 256 sequences); when the call's kernels finish (stream order), the
+ * area holds every rank's slice. Waits for peers are bounded (10 s; a
+ * timeout is reported by tl_sync_check as TL_ERR_DEVICE_FAULT). */
+int tl_decode_attention_peer(tl_cache *cache, int layer, const void *q, const int *seq_ids,
+                             int num_seqs, float scale, size_t out_offset, unsigned epoch,
+                             tl_stream_t stream);
+
 /* A paged KV pool that lives in memory the caller owns, laid out as the
  * handle's pool: fp16 [num_layers][2 (K,V)][num_blocks][block], each block
  * [block_size][Hkv][D] (token-major) or [Hkv][block_size][D] (head-major);

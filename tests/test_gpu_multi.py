@@ -82,6 +82,28 @@ def _rank(rank, world, port, q_out):
             for i in range(len(lens)):
                 ref = O.decode_one(q[i], full_k[(i, l)], full_v[(i, l)], scale)
                 check_close(got[i], ref, f"rank {rank} layer {l} seq {i}")
+        # the same layers through the NVLink peer-store gather
+        from gpu_helpers import d2h
+        slice_bytes = len(lens) * sl.q_count * D * 2
+        TD.connect_peer_gather(cache, L * world * slice_bytes)
+        gptr, _ = cache.peer_buffer()
+        dist.barrier()  # both ranks reach the GPU-side waits together
+        qkeep = []
+        for l in range(L):
+            q = O.normal_f16((len(lens), Hq, D), 77 + l)
+            qs = to_dev(np.ascontiguousarray(q[:, sl.q_first: sl.q_first + sl.q_count]))
+            qkeep.append(qs)
+            cache.decode_attention_peer(l, qs.data_ptr(), sids, l * world * slice_bytes, l + 1, scale)
+        cache.sync_check()
+        for l in range(L):
+            q = O.normal_f16((len(lens), Hq, D), 77 + l)
+            g = d2h(gptr + l * world * slice_bytes, world * slice_bytes // 2)
+            full = g.reshape(world, len(lens), sl.q_count, D).transpose(1, 0, 2, 3).reshape(len(lens), Hq, D)
+            got = O.f16_to_f32(np.ascontiguousarray(full))
+            for i in range(len(lens)):
+                ref = O.decode_one(q[i], full_k[(i, l)], full_v[(i, l)], scale)
+                check_close(got[i], ref, f"peer gather: rank {rank} layer {l} seq {i}")
+        dist.barrier()
         cache.close()
         dist.destroy_process_group()
         q_out.put((rank, "ok"))

@@ -20,6 +20,8 @@ enum DeviceErrorBits : int {
 constexpr int kMaxAppendRows = 256;
 constexpr int kMaxDeltas = 96;
 constexpr int kMaxDecodeSeqs = 256;
+constexpr int kMaxPeers = 8;  // GPUs of one node in a head-sharded group
+constexpr size_t kPeerFlagBytes = 256;  // flags area at the start of a peer region
 // Decode work item: 16 tokens of one KV head (a block of 32 is two items).
 constexpr int kDecodeTile = 16;
 // Units cut into more pieces than this are merged by the wide merge pass.
@@ -81,6 +83,21 @@ struct DecodeArgs {
     float *partial;         // [V][2][G][D+4] fp32 split partials (acc[D], m, l, pad)
     int *counters;          // [nseq][Hkv] zeroed tickets: the last worker of a cut
                             // unit merges it in-kernel; nullptr -> launch_merge pass
+    // Head-sharded peer mode (ndst > 0): outputs go to out_dst[r] instead of
+    // o (the host passes this rank's slice of its own gather area); the last
+    // CTA of the merge pass stores `epoch` to flag_dst[r] (this rank's flag).
+    // done_counter is a zeroed ticket, rearmed by the last CTA.
+    int ndst;
+    void *out_dst[kMaxPeers];
+    unsigned *flag_dst[kMaxPeers];
+    unsigned epoch;
+    int *done_counter;
+    // ... and the merge pass's last CTA then pulls the other ranks' slices:
+    // peer_base[r] = rank r's region (this rank's own at [rank]); slices sit
+    // at gather_off + r * slice_bytes in every region.
+    const unsigned char *peer_base[kMaxPeers];
+    int world, rank;
+    unsigned long long gather_off, slice_bytes;
     int layer;
     int group;              // G = Hq / Hkv
     float scale_log2;       // softmax scale * log2(e)
@@ -103,5 +120,6 @@ cudaError_t launch_apply_deltas(const DeltaArgs &a, cudaStream_t s);
 cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128);
 cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t s);
 cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s);
+
 
 }  // namespace tllm

@@ -48,6 +48,10 @@ constexpr int kTile = kDecodeTile;  // tokens per item
 constexpr int kWarps = 4;          // workers per CTA
 constexpr int kSmemBudget = 160 * 1024;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// A peer rank may legitimately start a layer seconds later than this one
+// (host-side skew at start-up); its flag wait gives up after 10 s.
+constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;
+constexpr int kMergeThreads = 512;  // wide merge CTA: 2 per SM, so a grid fits one wave
 
 template <int D>
 struct Cfg {
@@ -57,7 +61,8 @@ struct Cfg {
     static constexpr int kNS0 = kSmemBudget / (kWarps * kStageBytes);
     static constexpr int kNS = kNS0 < 2 ? 2 : (kNS0 > 8 ? 8 : kNS0);
     static constexpr int kRingBytes = kNS * kStageBytes;
-    static constexpr int kSmemBytes = kWarps * kRingBytes + kWarps * kNS * 8 + 1024;
+    static constexpr int kOutBytes = 8 * D * 2;           // one unit's fp16 output (G <= 8)
+    static constexpr int kSmemBytes = kWarps * kRingBytes + kWarps * kOutBytes + kWarps * kNS * 8 + 1024;
     static constexpr int kKS = D / 16;                    // k-steps of the QK mma
 };
 
@@ -70,6 +75,134 @@ struct ItemPos {
     int b, kvh, tile, nb;
     long long unit_first;
 };
+
+// Output stores. Without peers the output goes to a.o; in the head-sharded
+// peer mode every element is written to the same offset of each rank's
+// gather buffer (this rank's slice), over NVLink for the remote ones.
+__device__ __forceinline__ void store_out16(const DecodeArgs &a, long long off, uint4 v) {
+    if (a.ndst == 0) {
+        __half *p = static_cast<__half *>(a.o) + off;
+        if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+            *reinterpret_cast<uint4 *>(p) = v;
+        } else {  // outputs are only promised 4-byte alignment
+            uint32_t *q = reinterpret_cast<uint32_t *>(p);
+            q[0] = v.x; q[1] = v.y; q[2] = v.z; q[3] = v.w;
+        }
+        return;
+    }
+    for (int r = 0; r < a.ndst; ++r) *reinterpret_cast<uint4 *>(static_cast<__half *>(a.out_dst[r]) + off) = v;
+}
+
+// 4 halves: one 8-byte store per peer (peer buffers are 16-byte aligned),
+// two 4-byte stores locally (outputs are only promised 4-byte alignment).
+__device__ __forceinline__ void store_out8(const DecodeArgs &a, long long off, __half2 lo, __half2 hi) {
+    if (a.ndst == 0) {
+        __half *p = static_cast<__half *>(a.o) + off;
+        *reinterpret_cast<__half2 *>(p) = lo;
+        *reinterpret_cast<__half2 *>(p + 2) = hi;
+        return;
+    }
+    uint2 v;
+    v.x = *reinterpret_cast<uint32_t *>(&lo);
+    v.y = *reinterpret_cast<uint32_t *>(&hi);
+    for (int r = 0; r < a.ndst; ++r) *reinterpret_cast<uint2 *>(static_cast<__half *>(a.out_dst[r]) + off) = v;
+}
+
+__device__ __forceinline__ void store_out4(const DecodeArgs &a, long long off, __half2 v) {
+    if (a.ndst == 0) {
+        *reinterpret_cast<__half2 *>(static_cast<__half *>(a.o) + off) = v;
+        return;
+    }
+    for (int r = 0; r < a.ndst; ++r) *reinterpret_cast<__half2 *>(static_cast<__half *>(a.out_dst[r]) + off) = v;
+}
+
+// Raises this rank's flag on every peer once all of a launch's outputs are
+// visible system-wide: called by each finishing participant; the last one
+// (ticket == participants - 1) fences and publishes the epoch, then rearms.
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Publishes a launch's outputs in peer mode. Outputs are written to this
+// GPU's own gather area; each participant (one thread, after a barrier that
+// orders its outputs before it) takes a ticket with a gpu-scope release;
+// the last one then performs ONE system-scope release store of the epoch
+// into this rank's flag, so readers on other GPUs that acquire the flag see
+// every participant's outputs (causality through the ticket chain).
+__device__ __forceinline__ bool signal_peers(const DecodeArgs &a, int participants) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.done_counter) : "memory");
+    if (old == participants - 1) {
+        for (int r = 0; r < a.ndst; ++r)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flag_dst[r]), "r"(a.epoch) : "memory");
+        *a.done_counter = 0;  // rearmed; the next launch is ordered after this one
+        return true;
+    }
+    return false;
+}
+
+// After publishing, the last CTA gathers the other ranks' slices of the same
+// call into this rank's gather area. Lanes of warp 0 poll one peer flag each
+// over NVLink (relaxed polls, one acquire fence once every epoch is seen;
+// bounded), then the whole CTA copies all peers' slices in one loop with
+// independent 16-byte loads in flight. Publishing never waits, so two ranks
+// can never wait on each other.
+__device__ void pull_peer_slices(const DecodeArgs &a) {
+    __shared__ int s_ok;
+    constexpr int kBatch = 8;
+    if (threadIdx.x < 32) {
+        const int r = threadIdx.x;
+        int ok = 1;
+        if (r < a.world && r != a.rank) {
+            const unsigned *flag = reinterpret_cast<const unsigned *>(a.peer_base[r]) + r;
+            const uint64_t t0 = ptx::globaltimer_ns();
+            for (;;) {
+                unsigned v;
+                asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+                if ((int)(v - a.epoch) >= 0) break;
+                if (ptx::globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+                    atomicOr(a.g.err, kErrWaitTimeout);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (threadIdx.x == 0) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            s_ok = ok;
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    // all peers' slices as one index space of 16-byte chunks
+    const size_t n16 = a.slice_bytes / 16;
+    const size_t total = n16 * (size_t)(a.world - 1);
+    const size_t stride = blockDim.x;
+    unsigned char *local = const_cast<unsigned char *>(a.peer_base[a.rank]);
+    for (size_t base = threadIdx.x; base < total; base += stride * kBatch) {
+        uint4 v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const size_t i = base + j * stride;
+            if (i < total) {
+                int r = (int)(i / n16);
+                r += r >= a.rank;  // skip this rank's own slice
+                const size_t off = a.gather_off + (size_t)r * a.slice_bytes + (i % n16) * 16;
+                v[j] = __ldcg(reinterpret_cast<const uint4 *>(a.peer_base[r] + off));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const size_t i = base + j * stride;
+            if (i < total) {
+                int r = (int)(i / n16);
+                r += r >= a.rank;
+                const size_t off = a.gather_off + (size_t)r * a.slice_bytes + (i % n16) * 16;
+                *reinterpret_cast<uint4 *>(local + off) = v[j];
+            }
+        }
+    }
+}
 
 // Maps a flat item index to (sequence, kv_head, tile). prefix[] lives in the
 // kernel's parameter space; the search is uniform across the warp.
@@ -169,14 +302,13 @@ __device__ __forceinline__ void merge_unit(const DecodeArgs &a, long long unit_f
         M = Mn;
     }
     const float inv = 1.f / L;
-    __half *o = static_cast<__half *>(a.o) + ((long long)b * Hq + (long long)kvh * G + g) * D;
+    const long long obase = ((long long)b * Hq + (long long)kvh * G + g) * D;
 #pragma unroll
     for (int k = 0; k < kMaxChunks; ++k) {
         const int c = sub + k * lpg;
         if (k < nchunks && c < D / 4) {
-            // two 4-byte stores: the API only promises 4-byte aligned outputs
-            *reinterpret_cast<__half2 *>(o + 4 * c) = __floats2half2_rn(O[k].x * inv, O[k].y * inv);
-            *reinterpret_cast<__half2 *>(o + 4 * c + 2) = __floats2half2_rn(O[k].z * inv, O[k].w * inv);
+            store_out8(a, obase + 4 * c, __floats2half2_rn(O[k].x * inv, O[k].y * inv),
+                       __floats2half2_rn(O[k].z * inv, O[k].w * inv));
         }
     }
 }
@@ -206,7 +338,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     const PoolGeom &g = a.g;
     const int H = g.num_kv_heads, G = a.group, Hq = H * G, BS = g.block_size;
     uint8_t *ring = smem + warp * C::kRingBytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWarps * C::kRingBytes) + warp * C::kNS;
+    __half *ostage = reinterpret_cast<__half *>(smem + kWarps * C::kRingBytes + warp * C::kOutBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWarps * (C::kRingBytes + C::kOutBytes)) + warp * C::kNS;
     const uint32_t ring_u32 = ptx::smem_u32(ring);
     const uint32_t bar_u32 = ptx::smem_u32(bars);
 
@@ -296,6 +429,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     long long ufirst = 0;
     bool first_piece = true;
     bool failed = false;
+    bool wrote_remote = false;  // peer mode: this worker stored outputs to peers
 
     // Writes the finished unit (complete -> fp16 output; cut -> partial).
     auto finalize = [&]() {
@@ -308,20 +442,27 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         const bool complete = ufirst >= ws && ufirst + unb <= we;
         const int g0 = 2 * tig, g1 = 2 * tig + 1;
         if (complete) {
-            __half *o = static_cast<__half *>(a.o) + ((long long)ub * Hq + (long long)ukvh * G) * D;
+            // stage the unit's [G][D] fp16 output in shared memory, then
+            // write it out as coalesced 16-byte chunks
             const float i0 = 1.f / lt0, i1 = 1.f / lt1;
 #pragma unroll
             for (int dm = 0; dm < C::kKS; ++dm) {
                 const int d = dm * 16 + gid;
                 if (g0 < G) {
-                    o[(long long)g0 * D + d] = __float2half_rn(acc[dm][0] * i0);
-                    o[(long long)g0 * D + d + 8] = __float2half_rn(acc[dm][2] * i0);
+                    ostage[g0 * D + d] = __float2half_rn(acc[dm][0] * i0);
+                    ostage[g0 * D + d + 8] = __float2half_rn(acc[dm][2] * i0);
                 }
                 if (g1 < G) {
-                    o[(long long)g1 * D + d] = __float2half_rn(acc[dm][1] * i1);
-                    o[(long long)g1 * D + d + 8] = __float2half_rn(acc[dm][3] * i1);
+                    ostage[g1 * D + d] = __float2half_rn(acc[dm][1] * i1);
+                    ostage[g1 * D + d + 8] = __float2half_rn(acc[dm][3] * i1);
                 }
             }
+            __syncwarp();
+            const long long obase = ((long long)ub * Hq + (long long)ukvh * G) * D;
+            for (int ch = lane; ch < G * D / 8; ch += 32)
+                store_out16(a, obase + ch * 8, reinterpret_cast<const uint4 *>(ostage)[ch]);
+            __syncwarp();
+            wrote_remote = a.ndst > 0;
         } else {
             const int slot = first_piece ? 0 : 1;
             float *pbase = a.partial + ((worker * 2 + slot) * G) * (long long)kPartialRow<D>;
@@ -522,27 +663,26 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         return;
     }
     if (ub >= 0) finalize();
+    (void)wrote_remote;
 }
 
 // Second pass for launches without merge counters (and for units cut into
 // many pieces, where one warp would have to read hundreds of KB of
 // partials). One CTA per (unit, head): blockIdx.x = sequence*Hkv + kv_head,
-// blockIdx.y = head g of the group. Its 1024 threads are D/4 chunk lanes x
-// (4096/D) source groups; each group folds every kGroups-th source with an
+// blockIdx.y = head g of the group. Its 512 threads are D/4 chunk lanes x
+// (2048/D) source groups; each group folds every kGroups-th source with an
 // online softmax merge (independent loads), then the groups are combined in
 // shared memory. Complete units (one worker) were written by the decode
 // kernel and are skipped. Launched as a programmatic dependent of the decode
 // kernel: it waits for the decode grid before reading any partial.
 template <int D>
-__global__ void __launch_bounds__(1024) merge_kernel(const __grid_constant__ DecodeArgs a) {
+__device__ __forceinline__ void merge_body(const DecodeArgs &a) {
     constexpr int kRow = kPartialRow<D>;
     constexpr int kChunks = D / 4;
-    constexpr int kGroups = 1024 / kChunks;
+    constexpr int kGroups = kMergeThreads / kChunks;
     __shared__ float s_m[kGroups][kChunks];
     __shared__ float s_l[kGroups][kChunks];
     __shared__ float4 s_o[kGroups][kChunks];
-    ptx::griddep_launch_dependents();
-    ptx::griddep_wait();
     const int H = a.g.num_kv_heads, G = a.group, Hq = H * G;
     const int b = blockIdx.x / H, kvh = blockIdx.x % H, g = blockIdx.y;
     if (b >= a.nseq || g >= G) return;
@@ -589,9 +729,22 @@ __global__ void __launch_bounds__(1024) merge_kernel(const __grid_constant__ Dec
         Of.w += w * x.w;
     }
     const float inv = 1.f / Lf;
-    __half *o = static_cast<__half *>(a.o) + ((long long)b * Hq + (long long)kvh * G + g) * D + 4 * c;
-    *reinterpret_cast<__half2 *>(o) = __floats2half2_rn(Of.x * inv, Of.y * inv);
-    *reinterpret_cast<__half2 *>(o + 2) = __floats2half2_rn(Of.z * inv, Of.w * inv);
+    const long long off = ((long long)b * Hq + (long long)kvh * G + g) * D + 4 * c;
+    store_out8(a, off, __floats2half2_rn(Of.x * inv, Of.y * inv), __floats2half2_rn(Of.z * inv, Of.w * inv));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kMergeThreads, 2) merge_kernel(const __grid_constant__ DecodeArgs a) {
+    ptx::griddep_launch_dependents();
+    ptx::griddep_wait();
+    merge_body<D>(a);
+    if (a.done_counter) {  // peer mode: the last CTA publishes, then gathers
+        __shared__ int s_last;
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = signal_peers(a, gridDim.x * gridDim.y) ? 1 : 0;
+        __syncthreads();
+        if (s_last) pull_peer_slices(a);
+    }
 }
 
 // Opts the kernel into its dynamic shared memory size, once per device.
@@ -664,7 +817,7 @@ template <int D>
 cudaError_t launch_merge_t(const DecodeArgs &a, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nseq * a.g.num_kv_heads, a.group);
-    cfg.blockDim = dim3(1024);
+    cfg.blockDim = dim3(kMergeThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -514,6 +514,10 @@ void tl_destroy(tl_cache *c) {
         storage_free(c, c->rope_sin);
         storage_free(c, c->partial);
         storage_free(c, c->merge_counters);
+        for (int r = 0; r < tllm::kMaxPeers; ++r)
+            if (c->peer_opened[r]) cudaIpcCloseMemHandle(c->peer_bases[r]);
+        storage_free(c, c->peer_region);
+        storage_free(c, c->peer_done_counter);
     }
     delete c;
 }
@@ -766,87 +770,225 @@ int tl_permute_free_blocks(tl_cache *c, unsigned long long seed) {
     return TL_OK;
 }
 
-// Replacement for kernels::attention_decode (reference
-// kernels/attention.cu:114-128) as called at src/transformer.cpp:230-237.
-int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const int *seq_ids,
-                        int num_seqs, float scale, tl_stream_t stream_) {
-    if (!c) return TL_ERR_INVALID_ARG;
+}  // extern "C"
+
+namespace {
+
+// Where a head-sharded (peer-mode) decode writes and whom it signals.
+struct PeerSpec {
+    size_t out_offset;  // bytes into every rank's gathered area
+    unsigned epoch;
+};
+
+int decode_impl(tl_cache *c, const char *ctx, int layer, const void *q, void *o,
+                const int *seq_ids, int num_seqs, float scale, cudaStream_t stream,
+                const PeerSpec *peer) {
     if (layer < 0 || layer >= c->cfg.num_layers)
-        return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, "decodeAttention", layer));
-    if (num_seqs < 0) return set_error(c, TL_ERR_INVALID_ARG, "decodeAttention: num_seqs must be >= 0");
-    if (num_seqs == 0) return TL_OK;
+        return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, ctx, layer));
+    if (num_seqs < 0) return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": num_seqs must be >= 0");
+    if (num_seqs == 0 && !peer) return TL_OK;
     if (!q) return set_error(c, TL_ERR_INVALID_ARG, "query is null");
-    if (!o) return set_error(c, TL_ERR_INVALID_ARG, "output is null");
-    if (!seq_ids) return set_error(c, TL_ERR_INVALID_ARG, "seq_ids is null");
+    if (!o && !peer) return set_error(c, TL_ERR_INVALID_ARG, "output is null");
+    if (!seq_ids && num_seqs > 0) return set_error(c, TL_ERR_INVALID_ARG, "seq_ids is null");
     if (((uintptr_t)q & 3u) || ((uintptr_t)o & 3u))
-        return set_error(c, TL_ERR_INVALID_ARG, "decodeAttention: q and o must be 4-byte aligned");
+        return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": q and o must be 4-byte aligned");
     std::vector<const Sequence *> ss((size_t)num_seqs);
     for (int i = 0; i < num_seqs; ++i) {
         ss[(size_t)i] = find_seq(c, seq_ids[i]);
         if (!ss[(size_t)i])
             return set_error(c, TL_ERR_NOT_FOUND,
-                             "decodeAttention: sequence not found: " + std::to_string(seq_ids[i]));
+                             std::string(ctx) + ": sequence not found: " + std::to_string(seq_ids[i]));
     }
     if (!decode_geometry_supported(c))
         return set_error(c, TL_ERR_UNSUPPORTED,
-                         "decodeAttention: supported shapes are head_dim 64/128/256, block_size "
-                         "16/32, query group 1..8");
+                         std::string(ctx) + ": supported shapes are head_dim 64/128/256, block_size "
+                                            "16/32, query group 1..8");
     if (!c->on_device)
-        return set_error(c, TL_ERR_NO_DEVICE, "decodeAttention: handle has no CUDA device (bookkeeping backend)");
+        return set_error(c, TL_ERR_NO_DEVICE, std::string(ctx) + ": handle has no CUDA device (bookkeeping backend)");
+    const int D = c->cfg.head_dim, Hq = c->cfg.num_q_heads, Hkv = c->cfg.num_kv_heads;
+    const long long row = (long long)Hq * D;
+    if (peer) {
+        if (!c->peers_connected)
+            return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": peers are not connected (tl_peer_connect)");
+        if (num_seqs > tllm::kMaxDecodeSeqs)
+            return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": at most " +
+                                                        std::to_string(tllm::kMaxDecodeSeqs) +
+                                                        " sequences per peer-mode call");
+        const size_t slice = (size_t)num_seqs * (size_t)row * 2;
+        if ((peer->out_offset & 15u) ||
+            peer->out_offset + (size_t)c->peer_world * slice > c->gather_bytes)
+            return set_error(c, TL_ERR_INVALID_ARG,
+                             std::string(ctx) + ": out_offset must be 16-byte aligned and the "
+                                                "world's slices must fit the gather buffer");
+    }
     DeviceGuard guard(c);
-    cudaStream_t stream = (cudaStream_t)stream_;
     if (!c->pending.empty()) {
         int st = flush_deltas(c, stream);
         if (st != TL_OK) return st;
     }
-    const int D = c->cfg.head_dim, Hq = c->cfg.num_q_heads, Hkv = c->cfg.num_kv_heads;
     if (!(scale > 0.0f)) scale = 1.0f / std::sqrt((float)D);
-    const long long row = (long long)Hq * D;
-    for (int j0 = 0; j0 < num_seqs; j0 += tllm::kMaxDecodeSeqs) {
+    for (int j0 = 0; j0 < num_seqs || (peer && j0 == 0); j0 += tllm::kMaxDecodeSeqs) {
         const int n = std::min(tllm::kMaxDecodeSeqs, num_seqs - j0);
         tllm::DecodeArgs a{};
         a.g = c->geom();
         a.q = static_cast<const uint16_t *>(q) + j0 * row;
-        a.o = static_cast<uint16_t *>(o) + j0 * row;
+        a.o = peer ? nullptr : static_cast<uint16_t *>(o) + j0 * row;
         a.partial = c->partial;
         a.counters = c->merge_counters;  // in-kernel merge of cut units
         a.layer = layer;
         a.group = c->group;
         a.scale_log2 = scale * 1.4426950408889634f;
         a.nseq = n;
+        if (peer) {  // write this rank's slice locally, publish, pull the others
+            const size_t slice = (size_t)n * (size_t)row * 2;
+            unsigned char *base = static_cast<unsigned char *>(c->peer_region);
+            a.ndst = 1;
+            a.out_dst[0] = base + tllm::kPeerFlagBytes + peer->out_offset + (size_t)c->peer_rank * slice;
+            a.flag_dst[0] = reinterpret_cast<unsigned *>(base) + c->peer_rank;
+            a.epoch = peer->epoch;
+            for (int r = 0; r < c->peer_world; ++r)
+                a.peer_base[r] = static_cast<const unsigned char *>(c->peer_bases[r]);
+            a.world = c->peer_world;
+            a.rank = c->peer_rank;
+            a.gather_off = tllm::kPeerFlagBytes + peer->out_offset;
+            a.slice_bytes = slice;
+        }
         a.prefix[0] = 0;
         for (int i = 0; i < n; ++i) {
             const Sequence *s = ss[(size_t)(j0 + i)];
             a.slot[i] = s->slot;
             a.len[i] = s->written;
             a.prefix[i + 1] = a.prefix[i] + ceil_div(s->written, tllm::kDecodeTile);
-            if (s->written == 0) {
-                cudaError_t e = cudaMemsetAsync(static_cast<uint16_t *>(a.o) + (long long)i * row, 0,
-                                                (size_t)row * 2, stream);
-                if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: memset failed");
+            if (s->written == 0) {  // nothing to attend: zeros, as documented
+                const int ndst = peer ? a.ndst : 1;
+                for (int r = 0; r < ndst; ++r) {
+                    void *dst = peer ? static_cast<void *>(static_cast<uint16_t *>(a.out_dst[r]) + (long long)i * row)
+                                     : static_cast<void *>(static_cast<uint16_t *>(a.o) + (long long)i * row);
+                    cudaError_t e = cudaMemsetAsync(dst, 0, (size_t)row * 2, stream);
+                    if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: memset failed");
+                }
             }
         }
         a.total_items = (long long)Hkv * a.prefix[n];
-        if (a.total_items == 0) continue;
-        a.workers = (int)std::min<long long>(c->max_workers, a.total_items);
+        if (a.total_items == 0 && !peer) continue;
+        a.workers = (int)std::min<long long>(c->max_workers, std::max<long long>(a.total_items, 1));
         // Few long units cut into many pieces: merge them in a wide second
         // pass instead of by one warp inside the decode kernel.
         int max_tiles = 0;
         for (int i = 0; i < n; ++i) max_tiles = std::max(max_tiles, a.prefix[i + 1] - a.prefix[i]);
-        const long long pieces = (long long)max_tiles * a.workers / a.total_items + 2;
-        const bool two_pass = pieces > tllm::kInKernelMergeMaxPieces;
+        const long long pieces =
+            a.total_items ? (long long)max_tiles * a.workers / a.total_items + 2 : 0;
+        // peer mode: the merge pass always runs, its last CTA publishes and gathers
+        const bool two_pass = pieces > tllm::kInKernelMergeMaxPieces || a.total_items == 0 || peer;
         if (two_pass) a.counters = nullptr;
-        cudaError_t e = tllm::launch_decode(a, c->tmap, stream);
-        if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: decode launch failed");
-        ++c->launches;
+        cudaError_t e;
+        if (a.total_items > 0) {
+            tllm::DecodeArgs ad = a;
+            ad.done_counter = nullptr;
+            e = tllm::launch_decode(ad, c->tmap, stream);
+            if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: decode launch failed");
+            ++c->launches;
+        }
         if (two_pass) {
-            e = tllm::launch_merge(a, stream);
+            tllm::DecodeArgs am = a;
+            am.done_counter = peer ? c->peer_done_counter : nullptr;
+            e = tllm::launch_merge(am, stream);
             if (e != cudaSuccess) return cuda_fail(c, e, "decodeAttention: merge launch failed");
             ++c->launches;
         }
+        if (peer) break;
     }
     return TL_OK;
 }
+
+}  // namespace
+
+extern "C" {
+
+// Replacement for kernels::attention_decode (reference
+// kernels/attention.cu:114-128) as called at src/transformer.cpp:230-237.
+int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const int *seq_ids,
+                        int num_seqs, float scale, tl_stream_t stream) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    return decode_impl(c, "decodeAttention", layer, q, o, seq_ids, num_seqs, scale,
+                       (cudaStream_t)stream, nullptr);
+}
+
+int tl_peer_init(tl_cache *c, int rank, int world, size_t gather_bytes, void *ipc_handle) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    if (world < 1 || world > tllm::kMaxPeers || rank < 0 || rank >= world || !ipc_handle)
+        return set_error(c, TL_ERR_INVALID_ARG, "peerInit: need 1 <= world <= 8, 0 <= rank < world and a handle buffer");
+    if (!c->on_device)
+        return set_error(c, TL_ERR_NO_DEVICE, "peerInit: handle has no CUDA device (bookkeeping backend)");
+    if (c->peer_region)
+        return set_error(c, TL_ERR_INVALID_ARG, "peerInit: already initialised");
+    DeviceGuard guard(c);
+    const size_t bytes = tllm::kPeerFlagBytes + ((gather_bytes + 255) & ~size_t(255));
+    void *p = nullptr;
+    std::string why;
+    if (storage_alloc(c, &p, bytes, &why))
+        return set_error(c, TL_ERR_CUDA, "peerInit: allocation failed: " + why);
+    void *ctr = nullptr;
+    if (storage_alloc(c, &ctr, 256, &why)) {
+        storage_free(c, p);
+        return set_error(c, TL_ERR_CUDA, "peerInit: allocation failed: " + why);
+    }
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        storage_free(c, p);
+        storage_free(c, ctr);
+        return cuda_fail(c, e, "peerInit: cudaIpcGetMemHandle failed");
+    }
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    c->peer_region = p;
+    c->peer_done_counter = static_cast<int *>(ctr);
+    c->gather_bytes = bytes - tllm::kPeerFlagBytes;
+    c->peer_rank = rank;
+    c->peer_world = world;
+    return TL_OK;
+}
+
+int tl_peer_connect(tl_cache *c, const void *ipc_handles) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    if (!c->peer_region || !ipc_handles)
+        return set_error(c, TL_ERR_INVALID_ARG, "peerConnect: call tl_peer_init first and pass every rank's handle");
+    DeviceGuard guard(c);
+    const unsigned char *hs = static_cast<const unsigned char *>(ipc_handles);
+    for (int r = 0; r < c->peer_world; ++r) {
+        if (r == c->peer_rank) {
+            c->peer_bases[r] = c->peer_region;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hs + (size_t)r * TL_IPC_HANDLE_BYTES, sizeof(h));
+        void *p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_fail(c, e, "peerConnect: cudaIpcOpenMemHandle failed");
+        c->peer_bases[r] = p;
+        c->peer_opened[r] = true;
+    }
+    c->peers_connected = true;
+    return TL_OK;
+}
+
+int tl_peer_buffer(const tl_cache *c, void **gathered, size_t *bytes) {
+    if (!c || !gathered || !c->peer_region) return TL_ERR_INVALID_ARG;
+    *gathered = static_cast<unsigned char *>(c->peer_region) + tllm::kPeerFlagBytes;
+    if (bytes) *bytes = c->gather_bytes;
+    return TL_OK;
+}
+
+int tl_decode_attention_peer(tl_cache *c, int layer, const void *q, const int *seq_ids,
+                             int num_seqs, float scale, size_t out_offset, unsigned epoch,
+                             tl_stream_t stream) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    PeerSpec ps{out_offset, epoch};
+    return decode_impl(c, "decodeAttentionPeer", layer, q, nullptr, seq_ids, num_seqs, scale,
+                       (cudaStream_t)stream, &ps);
+}
+
+
 
 int tl_sync_check(tl_cache *c, tl_stream_t stream) {
     if (!c) return TL_ERR_INVALID_ARG;

@@ -77,6 +77,14 @@ struct tl_cache {
     float *rope_sin = nullptr;
     float *partial = nullptr;
     int *merge_counters = nullptr;  // [kMaxDecodeSeqs][Hkv], zero between launches
+    // head-sharded peer gather (one process per GPU, CUDA IPC mappings)
+    int peer_rank = -1, peer_world = 0;
+    void *peer_region = nullptr;      // [flags (kPeerFlagBytes)][gathered outputs]
+    size_t gather_bytes = 0;
+    int *peer_done_counter = nullptr;
+    void *peer_bases[tllm::kMaxPeers] = {};
+    bool peer_opened[tllm::kMaxPeers] = {};
+    bool peers_connected = false;
     size_t partial_floats = 0;
     int max_workers = 0;
     alignas(64) unsigned char tmap[128];

@@ -42,7 +42,8 @@ EXPORTED_SYMBOLS = [
     "tl_active_sequence_count", "tl_get_config", "tl_get_block_table", "tl_get_pool_stats",
     "tl_get_pool", "tl_decode_attention", "tl_sync_check", "tl_rope_table",
     "tl_permute_free_blocks", "tl_debug_inject_alloc_failure", "tl_version",
-    "tl_decode_attention_static",
+    "tl_decode_attention_static", "tl_peer_init", "tl_peer_connect", "tl_peer_buffer",
+    "tl_decode_attention_peer",
 ]
 
 
@@ -146,6 +147,10 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_version": (C.c_char_p, []),
         "tl_decode_attention_static": (i, [C.POINTER(PagedView), i, vp, vp, ip, ip, i, f, vp,
                                            C.c_char_p, i]),
+        "tl_peer_init": (i, [vp, i, i, sz, vp]),
+        "tl_peer_connect": (i, [vp, vp]),
+        "tl_peer_buffer": (i, [vp, C.POINTER(vp), C.POINTER(sz)]),
+        "tl_decode_attention_peer": (i, [vp, i, vp, ip, i, f, sz, C.c_uint, vp]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -287,6 +292,29 @@ class KVCache:
     def decode_attention(self, layer, q_ptr, o_ptr, seq_ids, scale=0.0, stream=0):
         self._check(self._lib.tl_decode_attention(self._h, int(layer), q_ptr, o_ptr, _ids(seq_ids),
                                                   len(seq_ids), float(scale), stream or None))
+
+    # -- head-sharded peer gather (one process per GPU) ----------------------
+    def peer_init(self, rank: int, world: int, gather_bytes: int) -> bytes:
+        """Allocates this rank's gather region; returns its 64-byte IPC handle."""
+        h = C.create_string_buffer(64)
+        self._check(self._lib.tl_peer_init(self._h, int(rank), int(world), int(gather_bytes), h))
+        return h.raw
+
+    def peer_connect(self, handles: list[bytes]) -> None:
+        blob = b"".join(handles)
+        buf = C.create_string_buffer(blob, len(blob))
+        self._check(self._lib.tl_peer_connect(self._h, buf))
+
+    def peer_buffer(self):
+        p, n = C.c_void_p(), C.c_size_t()
+        self._check(self._lib.tl_peer_buffer(self._h, C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def decode_attention_peer(self, layer, q_ptr, seq_ids, out_offset, epoch, scale=0.0, stream=0):
+        self._check(self._lib.tl_decode_attention_peer(self._h, int(layer), q_ptr, _ids(seq_ids),
+                                                       len(seq_ids), float(scale), int(out_offset),
+                                                       C.c_uint(epoch & 0xFFFFFFFF), stream or None))
+
 
     def sync_check(self, stream=0):
         self._check(self._lib.tl_sync_check(self._h, stream or None))

@@ -90,6 +90,19 @@ def gather_head_outputs(local_out, gathered, group=None) -> None:
     dist.all_gather_into_tensor(gathered.view(-1, *local.shape[1:]), local, group=group)
 
 
+def connect_peer_gather(cache, gather_bytes: int, group=None) -> None:
+    """Sets up the NVLink peer gather of a head-sharded cache: allocates this
+    rank's gather region, exchanges the CUDA IPC handles over the process
+    group (host objects only) and opens every peer's region."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    mine = cache.peer_init(rank, world, gather_bytes)
+    handles = [None] * world
+    dist.all_gather_object(handles, mine, group=group)
+    cache.peer_connect(handles)
+
+
 def rank_major_to_heads(gathered):
     """[N][B][Hq/N][D] -> [B][Hq][D] (reference-order view; copies)."""
     n, b, hq_local, d = gathered.shape
