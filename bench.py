@@ -57,6 +57,14 @@ CONFIGS = {
                rope=True, permute=True),
     "c4": dict(workload="c4 70B long-context GQA, 8 seqs @ ctx 32768 (1 GPU batch shard)",
                L=80, Hq=64, Hkv=8, D=128, bs=32, lens=[32768] * 8, rope=True),
+    # c5's steady-state decode batch as a static batch (diagnostic for c5):
+    # 225 sequences, lengths log-uniform in [32, 4096] + a geometric(256) tail
+    "c5s": dict(workload="c5 steady-state batch, static: 225 seqs, log-U[32,4096] prompts",
+                L=32, Hq=32, Hkv=8, D=128, bs=16, lens="loguniform", B=225, lo=32, hi=4096,
+                rope=True, permute=True),
+    "c5": dict(workload="c5 8B GQA continuous-batching churn: Poisson(4) arrivals, prompts "
+                        "log-U[32,4096], geometric(256) generations, <=256 active, pool ~80% occupied",
+               L=32, Hq=32, Hkv=8, D=128, bs=16, lens="churn", rope=True, permute=True),
 }
 
 
@@ -69,6 +77,12 @@ def peaks():
 
 
 def seq_lens(cfg, seed, rank):
+    if cfg["lens"] == "loguniform":
+        import numpy as np
+        rng = np.random.default_rng(seed + 1000 * rank)
+        lo, hi = math.log(cfg["lo"]), math.log(cfg["hi"])
+        return [int(round(math.exp(x))) + int(rng.geometric(1 / 256)) // 2
+                for x in rng.uniform(lo, hi, size=cfg["B"])]
     if cfg["lens"] == "ragged":
         import numpy as np
         rng = np.random.default_rng(seed + 1000 * rank)
@@ -359,6 +373,90 @@ def run_ours(cfg, args, world, rank, local):
     return res
 
 
+# ------------------------------------------------------------ churn (c5) --
+
+def run_churn(cfg, args, world, rank, local):
+    """Config 5: a continuous-batching schedule over args.warmup + args.steps
+    steps. Prompt prefill (per-layer appends) is timed apart from the decode
+    step (fused append + decode attention of every layer + advance), which
+    is what value / us_per_step measure."""
+    import torch
+    import tiny_llm_b200 as T
+    from tiny_llm_b200.churn import ChurnSchedule
+
+    L, Hq, Hkv, D, bs = cfg["L"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["bs"]
+    max_active, max_len = 256, 6144
+    nblocks = ChurnSchedule.pool_blocks_for(max_active, 32, 4096, 256, bs, occupancy=0.8)
+    cache = T.KVCache(num_layers=L, num_kv_heads=Hkv, head_dim=D, max_seq_len=max_len,
+                      max_batch_size=max_active, block_size=bs, num_blocks=nblocks, num_q_heads=Hq,
+                      rope_on_append=True, device=local)
+    cache.permute_free_blocks(args.seed + rank)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(args.seed * 7919 + rank)
+    prompt_kv = torch.randn((2, 4096, Hkv, D), dtype=torch.float16, device="cuda", generator=g)
+    step_k = torch.randn((L * max_active * Hkv * D,), dtype=torch.float16, device="cuda", generator=g)
+    step_v = torch.randn_like(step_k)
+    qbuf = torch.randn((L * max_active * Hq * D,), dtype=torch.float16, device="cuda", generator=g)
+    obuf = torch.empty_like(qbuf)
+    scale = 1.0 / math.sqrt(D)
+    sch = ChurnSchedule(seed=args.seed + rank, rate=4.0, max_active=max_active, block_size=bs)
+    ev_pairs, pf_pairs = [], []
+    timing = [False]
+
+    def prefill(sid, n):
+        if timing[0]:
+            a = torch.cuda.Event(enable_timing=True); a.record(stream); pf_pairs.append([a, None])
+        for l in range(L):
+            cache.append_kv(sid, l, prompt_kv[0].data_ptr(), prompt_kv[1].data_ptr(), n, sp)
+        cache.advance_seq_len(sid, n)
+        if timing[0]:
+            z = torch.cuda.Event(enable_timing=True); z.record(stream); pf_pairs[-1][1] = z
+
+    def decode_step(batch):
+        B = len(batch)
+        if timing[0]:
+            a = torch.cuda.Event(enable_timing=True); a.record(stream)
+        cache.append_kv_all_layers(batch, step_k.data_ptr(), step_v.data_ptr(), sp)
+        qv = qbuf[: L * B * Hq * D].view(L, B, Hq, D)
+        ov = obuf[: L * B * Hq * D].view(L, B, Hq, D)
+        for l in range(L):
+            cache.decode_attention(l, qv[l].data_ptr(), ov[l].data_ptr(), batch, scale, sp)
+        for s in batch:
+            cache.advance_seq_len(s, 1)
+        if timing[0]:
+            z = torch.cuda.Event(enable_timing=True); z.record(stream); ev_pairs.append((a, z))
+
+    kv_total = 0
+    sampler = None
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            torch.cuda.synchronize()
+            sampler = ClockSampler(local)
+            time.sleep(0.3)
+            barrier(world)
+            timing[0] = True
+            launches0 = cache.pool_stats().kernel_launches
+            occ0, act0, steps0 = sch.stats.occupancy_sum, sch.stats.active_sum, sch.stats.steps
+        batch, attended = sch.step(cache, prefill, decode_step, max_len)
+        if timing[0]:
+            kv_total += sum(attended) * L * 2 * Hkv * D * 2
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    dec_ms = sum(a.elapsed_time(z) for a, z in ev_pairs)
+    pf_ms = sum(a.elapsed_time(z) for a, z in pf_pairs)
+    launches = cache.pool_stats().kernel_launches - launches0
+    cache.sync_check(sp)
+    n = sch.stats.steps - steps0
+    res = dict(ms=dec_ms, kv=kv_total, prefill_ms=pf_ms, clocks=clocks, launches=launches,
+               mean_active=(sch.stats.active_sum - act0) / n,
+               occupancy=(sch.stats.occupancy_sum - occ0) / n,
+               admitted=sch.stats.admitted, released=sch.stats.released,
+               preempted=sch.stats.preempted, pool_blocks=nblocks)
+    cache.close()
+    return res
+
+
 # ---------------------------------------------------------- reference path --
 
 def load_ref():
@@ -546,11 +644,17 @@ def main():
                     help="multi-GPU split: whole sequences per rank (weak scaling) or KV heads "
                          "per rank with an all-gather of outputs each layer (strong scaling)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the config's layer count (small profiling cases; "
+                         "every decode launch keeps the config's shape)")
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers > 0:
+        cfg["L"] = args.layers
+        cfg["workload"] += f" [{args.layers} layers]"
     world, rank, local = dist_setup()
     peak, peak_kind = peaks()
     base_config = {"workload": cfg["workload"], "layers": cfg["L"], "q_heads": cfg["Hq"],
@@ -565,7 +669,11 @@ def main():
                    "seed": args.seed}
 
     if args.impl == "reference":
-        res, why = run_reference(cfg, args, world, rank, local)
+        if args.config == "c5":
+            res, why = None, ("reference arm runs uniform-length configs only; the reference "
+                              "engine has no continuous batching (max_batch_size=1)")
+        else:
+            res, why = run_reference(cfg, args, world, rank, local)
         if res is None:
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
@@ -595,6 +703,33 @@ def main():
                             "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
                     "decode_kernel_gbs": round(kv / world / (res["dec_ms"] / 1e3) / 1e9, 1) if res["dec_ms"] else None,
                     "clocks": res["clocks"]}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    if args.config == "c5":
+        res = run_churn(cfg, args, world, rank, local)
+        ms = barrier_max(res["ms"], world)
+        kv = barrier_sum(res["kv"], world)
+        if rank == 0:
+            peak, peak_kind = peaks()
+            value = kv / (ms / 1e3) / 1e9
+            line = {"metric": "decode attn+append KV-read GB/s", "value": round(value, 2),
+                    "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": round(ms / args.steps, 4),
+                    "us_per_step": round(1e3 * ms / args.steps, 1),
+                    "pct_hbm_peak_per_gpu": round(100 * value / world / peak, 1),
+                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "dtype": "f16 (fp32 accumulate)",
+                    "data": "synthetic N(0,1) fp16, seeded churn schedule",
+                    "config": dict(base_config, mean_active=round(res["mean_active"], 1),
+                                   pool_occupancy=round(res["occupancy"], 3),
+                                   pool_blocks=res["pool_blocks"], admitted=res["admitted"],
+                                   released=res["released"], preempted=res["preempted"],
+                                   prefill_ms_total_timed_apart=round(res["prefill_ms"], 2)),
+                    "clocks": res["clocks"], "gpu_launches": res["launches"]}
             print(json.dumps(line), flush=True)
         if world > 1:
             import torch.distributed as dist
