@@ -166,7 +166,7 @@ extern "C" int tl_decode_attention_static(const tl_paged_view *view, int layer, 
                                 " has a length outside 0..bt_stride*block_size or a negative table row"));
         a.slot[i] = table_rows[i];
         a.len[i] = S;
-        a.prefix[i + 1] = a.prefix[i] + (S + tllm::kDecodeTile - 1) / tllm::kDecodeTile;
+        a.prefix[i + 1] = a.prefix[i] + tllm::unit_slots((S + tllm::kDecodeTile - 1) / tllm::kDecodeTile);
     }
     if (!v.error_word) {
         e = cudaMemsetAsync(scratch, 0, sizeof(int), stream);

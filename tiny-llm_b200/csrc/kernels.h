@@ -26,6 +26,11 @@ constexpr size_t kPeerFlagBytes = 256;  // flags area at the start of a peer reg
 constexpr int kDecodeTile = 16;
 // Units cut into more pieces than this are merged by the wide merge pass.
 constexpr int kInKernelMergeMaxPieces = 12;
+// Work slots charged to each (sequence, kv_head) unit on top of its tiles:
+// the unit's fixed cost (Q load, finalize, output) in tile-equivalents, so
+// that the stream-K split balances time, not just tiles.
+constexpr int kUnitOverheadSlots = 2;
+inline int unit_slots(int tiles) { return tiles > 0 ? tiles + kUnitOverheadSlots : 0; }
 
 // Pool geometry shared by every kernel.
 struct PoolGeom {
@@ -106,7 +111,7 @@ struct DecodeArgs {
     int workers;            // V
     int slot[kMaxDecodeSeqs];     // block-table row of each sequence
     int len[kMaxDecodeSeqs];      // attended tokens of each sequence
-    int prefix[kMaxDecodeSeqs + 1];  // prefix sums of 16-token tiles per sequence
+    int prefix[kMaxDecodeSeqs + 1];  // prefix sums of unit_slots(tiles) per sequence
 };
 
 // Sizes the kernels need from the host.

@@ -71,9 +71,19 @@ struct Cfg {
 template <int D>
 constexpr int kPartialRow = D + 4;
 
+// Position of a work slot. The work of a call is a list of slots in
+// sequence-major, then kv-head order; unit (b, kvh) owns us =
+// unit_slots(tiles of b) consecutive slots: kUnitOverheadSlots virtual slots
+// (no data: they stand for the unit's fixed cost — Q load, finalize — so
+// that equal slot ranges mean equal time) followed by its real 16-token
+// tiles. tile = slot - kUnitOverheadSlots (< 0: virtual).
 struct ItemPos {
-    int b, kvh, tile, nb;
-    long long unit_first;
+    int b, kvh, slot, us;
+    long long unit_first;  // first slot of the unit (its virtual slots)
+    __device__ __forceinline__ int tile() const { return slot - kUnitOverheadSlots; }
+    __device__ __forceinline__ int nb() const { return us - kUnitOverheadSlots; }
+    __device__ __forceinline__ long long real_first() const { return unit_first + kUnitOverheadSlots; }
+    __device__ __forceinline__ long long last() const { return unit_first + us - 1; }
 };
 
 // Output stores. Without peers the output goes to a.o; in the head-sharded
@@ -216,11 +226,11 @@ __device__ __forceinline__ ItemPos locate(const DecodeArgs &a, long long w) {
     }
     ItemPos p;
     p.b = lo;
-    p.nb = a.prefix[lo + 1] - a.prefix[lo];
-    const int r = (int)(w - (long long)H * a.prefix[lo]);  // < H * nb < 2^31
-    p.kvh = r / p.nb;
-    p.tile = r - p.kvh * p.nb;
-    p.unit_first = (long long)H * a.prefix[lo] + (long long)p.kvh * p.nb;
+    p.us = a.prefix[lo + 1] - a.prefix[lo];
+    const int r = (int)(w - (long long)H * a.prefix[lo]);  // < H * us < 2^31
+    p.kvh = r / p.us;
+    p.slot = r - p.kvh * p.us;
+    p.unit_first = (long long)H * a.prefix[lo] + (long long)p.kvh * p.us;
     return p;
 }
 
@@ -361,30 +371,46 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     // ---- producer side: lane j of a batch describes item (base + j) ------
     struct Batch {
         int bid, kvh, sub;
+        unsigned real;  // ballot: lanes whose slot is a real tile of this range
     };
     auto load_batch = [&](long long base) {
-        Batch r{0, 0, 0};
+        Batch r{0, 0, 0, 0u};
         const long long w = base + lane;
+        bool is_real = false;
         if (w < we) {
             const ItemPos p = locate(a, w);
-            const int tok0 = p.tile * kTile;
-            const int slot = a.slot[p.b];
-            int bid = __ldg(g.block_tables + (long long)slot * g.bt_stride + tok0 / BS);
-            if (bid < 0 || bid >= g.num_blocks) {
-                atomicOr(g.err, kErrBlockRange);
-                bid = 0;  // stay in bounds; the call reports the error
+            if (p.tile() >= 0) {
+                is_real = true;
+                const int tok0 = p.tile() * kTile;
+                const int slot = a.slot[p.b];
+                int bid = __ldg(g.block_tables + (long long)slot * g.bt_stride + tok0 / BS);
+                if (bid < 0 || bid >= g.num_blocks) {
+                    atomicOr(g.err, kErrBlockRange);
+                    bid = 0;  // stay in bounds; the call reports the error
+                }
+                r.bid = bid;
+                r.kvh = p.kvh;
+                r.sub = tok0 % BS;
             }
-            r.bid = bid;
-            r.kvh = p.kvh;
-            r.sub = tok0 % BS;
         }
+        r.real = __ballot_sync(0xffffffffu, is_real);
         return r;
     };
+    long long cur_base = ws;
     Batch cur = load_batch(ws);
     Batch nxt = load_batch(ws + 32);
-    int issued = 0;
-    auto issue_one = [&]() {
-        const int j = issued & 31;
+    int issued = 0;  // real tiles issued; stage = issued % kNS
+    // Issues the next real tile of the range (uniform across the warp);
+    // false when the range has none left.
+    auto issue_one = [&]() -> bool {
+        while (cur.real == 0u) {
+            if (cur_base + 32 >= we) return false;
+            cur_base += 32;
+            cur = nxt;
+            nxt = load_batch(cur_base + 32);
+        }
+        const int j = __ffs(cur.real) - 1;
+        cur.real &= cur.real - 1u;
         const int bid = __shfl_sync(0xffffffffu, cur.bid, j);
         const int kvh = __shfl_sync(0xffffffffu, cur.kvh, j);
         const int sub = __shfl_sync(0xffffffffu, cur.sub, j);
@@ -412,20 +438,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
             }
         }
         ++issued;
-        if ((issued & 31) == 0) {
-            cur = nxt;
-            nxt = load_batch(ws + issued + 32);
-        }
+        return true;
     };
 
-    const int prologue = count < C::kNS ? count : C::kNS;
-    for (int i = 0; i < prologue; ++i) issue_one();
+    for (int i = 0; i < C::kNS; ++i)
+        if (!issue_one()) break;
 
     // ---- consumer state for the current (sequence, kv_head) unit ---------
     uint32_t qf[C::kKS][2];
     float acc[C::kKS][4];  // O^T tiles: d in [16*dm, 16*dm+16), g in {2tig, 2tig+1}
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    int ub = -1, ukvh = -1, unb = 0;
+    int ub = -1, ukvh = -1, uus = 0;
     long long ufirst = 0;
     bool first_piece = true;
     bool failed = false;
@@ -439,7 +462,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
             lt0 += __shfl_xor_sync(0xffffffffu, lt0, off);
             lt1 += __shfl_xor_sync(0xffffffffu, lt1, off);
         }
-        const bool complete = ufirst >= ws && ufirst + unb <= we;
+        const bool complete = ufirst + kUnitOverheadSlots >= ws && ufirst + uus <= we;
         const int g0 = 2 * tig, g1 = 2 * tig + 1;
         if (complete) {
             // stage the unit's [G][D] fp16 output in shared memory, then
@@ -493,8 +516,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
                 // an atomic ticket, no waiting on other workers.
                 __threadfence();
                 __syncwarp();
-                const long long v_first = worker_of_item(ufirst, W, V);
-                const long long v_last = worker_of_item(ufirst + unb - 1, W, V);
+                const long long v_first = worker_of_item(ufirst + kUnitOverheadSlots, W, V);
+                const long long v_last = worker_of_item(ufirst + uus - 1, W, V);
                 int *ctr = a.counters + ((long long)ub * H + ukvh);
                 int last = 0;
                 if (lane == 0) last = atomicAdd(ctr, 1) == (int)(v_last - v_first);
@@ -510,29 +533,32 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     };
 
     ItemPos p = locate(a, ws);
-    bool new_unit = true;
+    long long w = ws;  // current slot; virtual slots are jumped over
+    if (p.slot < kUnitOverheadSlots) {
+        w += kUnitOverheadSlots - p.slot;
+        p.slot = kUnitOverheadSlots;
+    }
     int fail_at = -1;
-    for (int i = 0; i < count; ++i) {
-        if (i > 0) {  // advance (sequence, kv_head, tile) by one item
-            if (++p.tile == p.nb) {
-                p.tile = 0;
-                p.unit_first += p.nb;
-                if (++p.kvh == H) {
-                    p.kvh = 0;
-                    do {
-                        ++p.b;
-                        p.nb = a.prefix[p.b + 1] - a.prefix[p.b];
-                    } while (p.nb == 0);
-                }
-                new_unit = true;
+    int k = 0;  // real tiles consumed; stage = k % kNS
+    for (; w < we; ++w) {
+        if (p.slot == p.us) {  // next unit; its virtual slots are skipped
+            p.unit_first += p.us;
+            if (++p.kvh == H) {
+                p.kvh = 0;
+                do {
+                    ++p.b;
+                    p.us = a.prefix[p.b + 1] - a.prefix[p.b];
+                } while (p.us == 0);
             }
+            p.slot = kUnitOverheadSlots;
+            w += kUnitOverheadSlots;
+            if (w >= we) break;
         }
-        if (new_unit) {
-            new_unit = false;
+        if (p.b != ub || p.kvh != ukvh) {
             if (ub >= 0) finalize();
             ub = p.b;
             ukvh = p.kvh;
-            unb = p.nb;
+            uus = p.us;
             ufirst = p.unit_first;
             // Q fragments (B operand, col-major 16x8): rows d, cols g = gid.
             const __half *qrow = static_cast<const __half *>(a.q) +
@@ -553,17 +579,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
             l0 = l1 = 0.f;
         }
 
-        const int stage = i % C::kNS;
-        const uint32_t parity = (uint32_t)((i / C::kNS) & 1);
+        const int stage = k % C::kNS;
+        const uint32_t parity = (uint32_t)((k / C::kNS) & 1);
         if (!ptx::mbar_wait_bounded(bar_u32 + 8 * stage, parity, kWaitLimitNs)) {
             if (lane == 0) atomicOr(g.err, kErrWaitTimeout);
             failed = true;
-            fail_at = i;
+            fail_at = k;
             break;
         }
         const uint32_t kbase = ring_u32 + stage * C::kStageBytes;
         const uint32_t vbase = kbase + C::kNSub * C::kSubBytes;
-        const int nvalid = min(kTile, a.len[p.b] - p.tile * kTile);
+        const int nvalid = min(kTile, a.len[p.b] - p.tile() * kTile);
 
         // ---- S^T = K Q^T (two accumulators to shorten the mma chain) ----
         float s_even[4] = {0.f, 0.f, 0.f, 0.f}, s_odd[4] = {0.f, 0.f, 0.f, 0.f};
@@ -644,7 +670,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
             }
         }
         __syncwarp();
-        if (issued < count) issue_one();
+        ++k;
+        ++p.slot;
+        issue_one();
     }
 
     if (failed) {
@@ -686,12 +714,12 @@ __device__ __forceinline__ void merge_body(const DecodeArgs &a) {
     const int H = a.g.num_kv_heads, G = a.group, Hq = H * G;
     const int b = blockIdx.x / H, kvh = blockIdx.x % H, g = blockIdx.y;
     if (b >= a.nseq || g >= G) return;
-    const int nb = a.prefix[b + 1] - a.prefix[b];
-    if (nb == 0) return;
+    const int us = a.prefix[b + 1] - a.prefix[b];
+    if (us == 0) return;
     const long long W = a.total_items, V = a.workers;
-    const long long unit_first = (long long)H * a.prefix[b] + (long long)kvh * nb;
-    const long long v_first = worker_of_item(unit_first, W, V);
-    const long long v_last = worker_of_item(unit_first + nb - 1, W, V);
+    const long long unit_first = (long long)H * a.prefix[b] + (long long)kvh * us;
+    const long long v_first = worker_of_item(unit_first + kUnitOverheadSlots, W, V);
+    const long long v_last = worker_of_item(unit_first + us - 1, W, V);
     if (v_first == v_last) return;
     const int c = threadIdx.x % kChunks, sg = threadIdx.x / kChunks;
     float M = -INFINITY, L = 0.f;

@@ -858,7 +858,7 @@ int decode_impl(tl_cache *c, const char *ctx, int layer, const void *q, void *o,
             const Sequence *s = ss[(size_t)(j0 + i)];
             a.slot[i] = s->slot;
             a.len[i] = s->written;
-            a.prefix[i + 1] = a.prefix[i] + ceil_div(s->written, tllm::kDecodeTile);
+            a.prefix[i + 1] = a.prefix[i] + tllm::unit_slots(ceil_div(s->written, tllm::kDecodeTile));
             if (s->written == 0) {  // nothing to attend: zeros, as documented
                 const int ndst = peer ? a.ndst : 1;
                 for (int r = 0; r < ndst; ++r) {
