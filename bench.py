@@ -16,7 +16,8 @@ block 16, RoPE theta 10000 on K at append. KV bytes read per step ~34.4 GB
   value     aggregate KV-read GB/s over all ranks (sum of KV bytes / max time)
   e2e       same metric through the C-ABI with per-step pinned-host H2D of
             the step's Q/K/V and D2H of its outputs inside the timed region
-  roofline  decode kernel: algorithmic bytes per launch / CUDA-event time
+  roofline  decode kernel: algorithmic bytes per launch / CUDA-event time,
+            from a pass after the timed steps with events around each layer
   cpu_baseline  the CPU oracle (fp32, OpenMP) on a bounded sample
 
 --impl reference runs the reference's own path instead (oracle/_ref:
@@ -57,6 +58,10 @@ CONFIGS = {
                rope=True, permute=True),
     "c4": dict(workload="c4 70B long-context GQA, 8 seqs @ ctx 32768 (1 GPU batch shard)",
                L=80, Hq=64, Hkv=8, D=128, bs=32, lens=[32768] * 8, rope=True),
+    # one rank's slice of c4 head-sharded over 8 GPUs (1 KV head, its 8 query
+    # heads, all 8 sequences): the local work of that mode, on one GPU
+    "c4r8": dict(workload="c4 per-rank slice of the 8-way head shard (1 KV head, 8 q heads)",
+                 L=80, Hq=8, Hkv=1, D=128, bs=32, lens=[32768] * 8, rope=True),
     # c5's steady-state decode batch as a static batch (diagnostic for c5):
     # 225 sequences, lengths log-uniform in [32, 4096] + a geometric(256) tail
     "c5s": dict(workload="c5 steady-state batch, static: 225 seqs, log-U[32,4096] prompts",
@@ -202,9 +207,10 @@ def run_ours(cfg, args, world, rank, local):
     B = len(lens)
     steps = args.warmup + args.steps
     e2e_steps = args.warmup + args.steps
-    max_len = max(lens) + steps + e2e_steps + 2
+    extra = steps + e2e_steps + args.steps + 2  # timed, e2e and roofline passes
+    max_len = max(lens) + extra
     layout = T.TL_LAYOUT_HEAD_MAJOR if args.layout == "head" else T.TL_LAYOUT_TOKEN_MAJOR
-    nblocks = sum(-(-(l + steps + e2e_steps + 2) // bs) for l in lens)
+    nblocks = sum(-(-(l + extra) // bs) for l in lens)
     cache = T.KVCache(num_layers=L, num_kv_heads=Hkv, head_dim=D, max_seq_len=max_len,
                       max_batch_size=B, block_size=bs, num_blocks=nblocks, num_q_heads=Hq,
                       rope_on_append=cfg["rope"], rope_theta=10000.0, layout=layout,
@@ -254,16 +260,32 @@ def run_ours(cfg, args, world, rank, local):
         if head and world > 1 and not p2p:  # the layer's outputs, all heads, on every rank
             TD.gather_head_outputs(out[b][l], gathered[l])
 
-    dec_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(L * args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kv_total = 0
-    dec_bytes = 0
     launches0 = None
     clocks = None
     sampler = None
+
+    def run_step(i, events=None):
+        nonlocal cur
+        b = i % nbuf
+        cache.append_kv_all_layers(sids, knew[b].data_ptr(), vnew[b].data_ptr(), sp)
+        attended = [c + 1 for c in cur]
+        for l in range(L):
+            if events is not None:
+                events[l][0].record(stream)
+            decode(b, l)
+            if events is not None:
+                events[l][1].record(stream)
+            after_decode(b, l)
+        for s in sids:
+            cache.advance_seq_len(s, 1)
+        cur = attended
+        return attended
+
+    # timed steps: no events between the layers (an event between two
+    # kernels would stop the next one from launching early)
     for i in range(steps):
-        timed = i >= args.warmup
         if i == args.warmup:
             torch.cuda.synchronize()
             sampler = ClockSampler(local)
@@ -271,30 +293,28 @@ def run_ours(cfg, args, world, rank, local):
             barrier(world)  # after the sampler starts: ranks enter the timed steps together
             launches0 = cache.pool_stats().kernel_launches
             start.record(stream)
-        b = i % nbuf
-        cache.append_kv_all_layers(sids, knew[b].data_ptr(), vnew[b].data_ptr(), sp)
-        attended = [c + 1 for c in cur]
-        for l in range(L):
-            if timed:
-                dec_ev[(i - args.warmup) * L + l][0].record(stream)
-            decode(b, l)
-            if timed:
-                dec_ev[(i - args.warmup) * L + l][1].record(stream)
-            after_decode(b, l)
-        for s in sids:
-            cache.advance_seq_len(s, 1)
-        cur = attended
-        if timed:
+        attended = run_step(i)
+        if i >= args.warmup:
             kv_total += kv_bytes(attended, kcfg)
-            dec_bytes += kv_bytes(attended, kcfg) + 2 * L * B * Hq * D * 2 + \
-                sum(-(-s // bs) for s in attended) * 4 * L
     end.record(stream)
     end.synchronize()
     launches = cache.pool_stats().kernel_launches - launches0
     if sampler:
         clocks = sampler.stop()
     ms = start.elapsed_time(end)
-    dec_ms = sum(a.elapsed_time(z) for a, z in dec_ev)
+    cache.sync_check(sp)
+
+    # roofline pass: the same steps again, with CUDA events around every
+    # layer's decode call (decode + in-kernel merge) on the launching stream
+    dec_ms, dec_bytes = 0.0, 0
+    for i in range(args.steps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(L)]
+        attended = run_step(steps + i, evs)
+        dec_bytes += kv_bytes(attended, kcfg) + 2 * L * B * Hq * D * 2 + \
+            sum(-(-s // bs) for s in attended) * 4 * L
+        torch.cuda.synchronize()
+        dec_ms += sum(a.elapsed_time(z) for a, z in evs)
     cache.sync_check(sp)
 
     # ---- e2e: host buffers, H2D of each step's inputs and D2H of its output
