@@ -100,7 +100,8 @@ class ClockSampler:
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,"
+              "clocks.mem,temperature.memory")
 
     def __init__(self, device_index: int):
         self.proc = None
@@ -136,8 +137,13 @@ class ClockSampler:
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        num = lambda v: float(v) if v.replace(".", "").isdigit() else None
+        mem = [num(r[9]) for r in rows if len(r) > 9 and num(r[9]) is not None]
+        hbm_t = [num(r[10]) for r in rows if len(r) > 10 and num(r[10]) is not None]
         return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows),
+                "mem_mhz": statistics.median(mem) if mem else None,
+                "hbm_temp_c": max(hbm_t) if hbm_t else None}
 
 
 def dist_setup():

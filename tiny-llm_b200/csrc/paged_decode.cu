@@ -358,10 +358,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         ptx::fence_barrier_init();
     }
     __syncwarp();
-    // Programmatic dependent launch: the next kernel in the stream may begin
-    // launching now (its CTAs only fit as ours retire); this kernel reads
-    // nothing from global memory before the previous grid has completed.
-    ptx::griddep_launch_dependents();
+    // Programmatic dependent launch. With the in-kernel merge the dependent is
+    // the next decode, whose CTAs only fit as ours retire: it may begin
+    // launching now. With the merge pass the dependent is that pass, whose
+    // CTAs would sit on our SMs and take issue slots while they wait: it is
+    // released only once this CTA's loads are done. This kernel reads nothing
+    // from global memory before the previous grid has completed.
+    const bool early_trigger = a.counters != nullptr;
+    if (early_trigger) ptx::griddep_launch_dependents();
     ptx::griddep_wait();
 
     const uint64_t policy = ptx::l2_policy_evict_first();
@@ -675,6 +679,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         issue_one();
     }
 
+    if (!early_trigger) ptx::griddep_launch_dependents();
     if (failed) {
         // Drain this worker's own loads still in flight (bounded) and stop.
         if (lane == 0) {
@@ -699,10 +704,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 // partials). One CTA per (unit, head): blockIdx.x = sequence*Hkv + kv_head,
 // blockIdx.y = head g of the group. Its 512 threads are D/4 chunk lanes x
 // (2048/D) source groups; each group folds every kGroups-th source with an
-// online softmax merge (independent loads), then the groups are combined in
-// shared memory. Complete units (one worker) were written by the decode
-// kernel and are skipped. Launched as a programmatic dependent of the decode
-// kernel: it waits for the decode grid before reading any partial.
+// online softmax merge, three sources per round with their loads issued
+// together (the 64-register budget of two CTAs per SM), then the groups are
+// combined in shared memory. Complete units (one worker) were written by the
+// decode kernel and are skipped. Launched as a programmatic dependent of the
+// decode kernel, which releases it once its loads are done: it waits for
+// the decode grid before reading any partial.
 template <int D>
 __device__ __forceinline__ void merge_body(const DecodeArgs &a) {
     constexpr int kRow = kPartialRow<D>;
@@ -724,18 +731,43 @@ __device__ __forceinline__ void merge_body(const DecodeArgs &a) {
     const int c = threadIdx.x % kChunks, sg = threadIdx.x / kChunks;
     float M = -INFINITY, L = 0.f;
     float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (long long u = v_first + sg; u <= v_last; u += kGroups) {
-        const int slot = worker_start(u, W, V) >= unit_first ? 0 : 1;
-        const float *pb = a.partial + ((u * 2 + slot) * G + g) * (long long)kRow;
-        const float m = __ldcg(pb + D), l = __ldcg(pb + D + 1);
-        const float4 x = __ldcg(reinterpret_cast<const float4 *>(pb) + c);
-        const float Mn = fmaxf(M, m);
-        const float sc = ptx::ex2(M - Mn), w = ptx::ex2(m - Mn);
-        L = L * sc + w * l;
-        O.x = O.x * sc + w * x.x;
-        O.y = O.y * sc + w * x.y;
-        O.z = O.z * sc + w * x.z;
-        O.w = O.w * sc + w * x.w;
+    // Sources sg, sg + kGroups, ...: the loads of a batch are issued together.
+    constexpr int kBatch = 3;
+    for (long long u0 = v_first + sg; u0 <= v_last; u0 += (long long)kGroups * kBatch) {
+        float mv[kBatch], lv[kBatch];
+        float4 xv[kBatch];
+#pragma unroll
+        for (int r = 0; r < kBatch; ++r) {
+            const long long u = u0 + (long long)r * kGroups;
+            mv[r] = -INFINITY;
+            lv[r] = 0.f;
+            xv[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (u <= v_last) {
+                const int slot = worker_start(u, W, V) >= unit_first ? 0 : 1;
+                const float *pb = a.partial + ((u * 2 + slot) * G + g) * (long long)kRow;
+                mv[r] = __ldcg(pb + D);
+                lv[r] = __ldcg(pb + D + 1);
+                xv[r] = __ldcg(reinterpret_cast<const float4 *>(pb) + c);
+            }
+        }
+        float Mn = M;
+#pragma unroll
+        for (int r = 0; r < kBatch; ++r) Mn = fmaxf(Mn, mv[r]);  // finite: source u0 exists
+        const float sc = ptx::ex2(M - Mn);  // M = -inf on the first batch: 0
+        L *= sc;
+        O.x *= sc;
+        O.y *= sc;
+        O.z *= sc;
+        O.w *= sc;
+#pragma unroll
+        for (int r = 0; r < kBatch; ++r) {
+            const float w = ptx::ex2(mv[r] - Mn);  // missing sources: -inf -> 0
+            L += w * lv[r];
+            O.x += w * xv[r].x;
+            O.y += w * xv[r].y;
+            O.z += w * xv[r].z;
+            O.w += w * xv[r].w;
+        }
         M = Mn;
     }
     s_m[sg][c] = M;
