@@ -658,14 +658,18 @@ def cpu_baseline(cfg, seed, budget_s=10.0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 20; c5: 2000 scheduler steps)")
+    ap.add_argument("--warmup", type=int, default=None,
+                    help="untimed steps first (default 5; c5: 300, until the schedule is "
+                         "at its steady state)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--layout", choices=["token", "head"], default="token")
     ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
-                    help="head-shard output exchange: NVLink peer stores from the decode "
-                         "epilogue, or an NCCL all-gather after each layer")
+                    help="head-shard output exchange: fused into the decode call (each rank "
+                         "publishes a flag, then pulls the other ranks' slices over NVLink), "
+                         "or an NCCL all-gather after each layer")
     ap.add_argument("--shard", choices=["batch", "head"], default="batch",
                     help="multi-GPU split: whole sequences per rank (weak scaling) or KV heads "
                          "per rank with an all-gather of outputs each layer (strong scaling)")
@@ -676,6 +680,10 @@ def main():
     ap.add_argument("--cpu-baseline-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 2000 if args.config == "c5" else 20
+    if args.warmup is None:
+        args.warmup = 300 if args.config == "c5" else 5
     args.warmup = max(args.warmup, 3)
     cfg = dict(CONFIGS[args.config])
     if args.layers > 0:
