@@ -254,8 +254,17 @@ def run_ours(cfg, args, world, rank, local):
     scale = 1.0 / math.sqrt(D)
     cur = list(lens)
 
+    layer_flow = args.flow == "layer"
+
+    def append_step(b):
+        if not layer_flow:  # one fused append of every layer's new token
+            cache.append_kv_all_layers(sids, knew[b].data_ptr(), vnew[b].data_ptr(), sp)
+
     def decode(b, l):
-        if p2p:  # decode + publish + pull of the other ranks' slices, fused
+        if layer_flow:  # TransformerLayer::attention: this layer's append, then decode (RoPE on Q)
+            cache.attention_step(l, q[b][l].data_ptr(), knew[b][l].data_ptr(), vnew[b][l].data_ptr(),
+                                 out[b][l].data_ptr(), sids, scale, sp)
+        elif p2p:  # decode + publish + pull of the other ranks' slices, fused
             epoch[0] += 1
             cache.decode_attention_peer(l, q[b][l].data_ptr(), sids, l * world * slice_bytes,
                                         epoch[0], scale, sp)
@@ -275,7 +284,7 @@ def run_ours(cfg, args, world, rank, local):
     def run_step(i, events=None):
         nonlocal cur
         b = i % nbuf
-        cache.append_kv_all_layers(sids, knew[b].data_ptr(), vnew[b].data_ptr(), sp)
+        append_step(b)
         attended = [c + 1 for c in cur]
         for l in range(L):
             if events is not None:
@@ -356,7 +365,7 @@ def run_ours(cfg, args, world, rank, local):
         for i in range(n):
             b = i % nbuf
             stream.wait_event(h2d_done[b])
-            cache.append_kv_all_layers(sids, knew[b].data_ptr(), vnew[b].data_ptr(), sp)
+            append_step(b)
             attended = [c + 1 for c in cur]
             for l in range(L):
                 decode(b, l)
@@ -673,6 +682,10 @@ def main():
     ap.add_argument("--shard", choices=["batch", "head"], default="batch",
                     help="multi-GPU split: whole sequences per rank (weak scaling) or KV heads "
                          "per rank with an all-gather of outputs each layer (strong scaling)")
+    ap.add_argument("--flow", choices=["fused", "layer"], default="fused",
+                    help="fused: one append of every layer's new token, then decode per layer; "
+                         "layer: per layer, append that layer's token then decode with RoPE on Q "
+                         "(the TransformerLayer::attention flow, tl_attention_step)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--layers", type=int, default=0,
                     help="override the config's layer count (small profiling cases; "
@@ -695,12 +708,17 @@ def main():
                    "kv_heads": cfg["Hkv"], "head_dim": cfg["D"], "block_size": cfg["bs"],
                    "rope_on_append": cfg["rope"], "layout": args.layout,
                    "parallelism": (f"head-shard x{world} (KV heads per GPU, outputs gathered per layer by "
-                                   + ("NVLink peer stores from the decode epilogue)" if args.gather == "p2p"
-                                      else "NCCL all-gather)")
+                                   + ("a flag publish and NVLink pull fused into the decode call)"
+                                      if args.gather == "p2p" else "NCCL all-gather)")
                                    if args.shard == "head" else
                                    f"batch-shard x{world} (independent sequences per GPU)"),
                    "l2": "KV bytes per step far above the 126 MB L2; no flush needed",
+                   "flow": ("per layer: append that layer's token, decode with RoPE on Q "
+                            "(tl_attention_step)" if args.flow == "layer" else
+                            "one fused append of all layers' tokens, then decode per layer"),
                    "seed": args.seed}
+    if args.flow == "layer" and (args.shard == "head" or args.config == "c5" or args.impl == "reference"):
+        raise SystemExit("--flow layer applies to the batch-sharded uniform/ragged configs of our arm")
 
     if args.impl == "reference":
         if args.config == "c5":

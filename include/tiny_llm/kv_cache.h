@@ -81,6 +81,12 @@ class KVCacheManager {
     Result<void> decodeAttention(int layer_idx, const half *q, half *out,
                                  const std::vector<int> &seq_ids, float scale = 0.0f,
                                  cudaStream_t stream = 0);
+    // The decode branch of TransformerLayer::attention for a batch: appendKV
+    // of each sequence's new token in layer_idx, then attention over len + 1
+    // tokens (Q rotated like K when the cache rotates on append).
+    Result<void> attentionStep(int layer_idx, const half *q, const half *k_new, const half *v_new,
+                               half *out, const std::vector<int> &seq_ids, float scale = 0.0f,
+                               cudaStream_t stream = 0);
     Result<std::vector<int>> getBlockTable(int seq_id) const;
     tl_pool_stats getPoolStats() const noexcept;
     Result<void> syncCheck(cudaStream_t stream = 0);

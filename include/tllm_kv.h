@@ -175,6 +175,18 @@ int tl_get_pool(const tl_cache *cache, void **base, size_t *elements);
 int tl_decode_attention(tl_cache *cache, int layer, const void *q, void *o, const int *seq_ids,
                         int num_seqs, float scale, tl_stream_t stream);
 
+/* The decode branch of TransformerLayer::attention (reference
+ * src/transformer.cpp:222-237: appendKV, then attention_decode over
+ * getSeqLen()+1 tokens) for a batch of sequences with one new token each:
+ * appends k_new/v_new ([num_seqs][Hkv][D] fp16, device) at each sequence's
+ * current length in `layer` (RoPE on K when the handle rotates on append),
+ * then decodes q ([num_seqs][Hq][D]) into o over len + 1 tokens, with Q
+ * rotated by the same table at the same position when K is. The caller
+ * advances every sequence once after its last layer (tl_advance_seq_len).
+ * Errors as tl_append_kv_all_layers and tl_decode_attention. */
+int tl_attention_step(tl_cache *cache, int layer, const void *q, const void *k_new, const void *v_new,
+                      void *o, const int *seq_ids, int num_seqs, float scale, tl_stream_t stream);
+
 /* ---- Head-sharded decode across the GPUs of one node -------------------
  * No reference counterpart (the reference is single-GPU). With KV heads
  * split over `world` ranks (one process per GPU), each rank's decode writes

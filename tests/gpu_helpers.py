@@ -153,6 +153,32 @@ class Run:
             worst = (max(worst[0], ma), max(worst[1], mr))
         return worst
 
+    def attention_step_and_check(self, layer, sids, seed, scale=None):
+        """tl_attention_step for one layer: appends one new token per
+        sequence, decodes with Q rotated like K, and checks the output
+        against the oracle (RoPE row on Q at the new token's position, fp64
+        attention over every token including the new one)."""
+        import torch
+        B = len(sids)
+        k = O.normal_f16((B, self.Hkv, self.D), seed)
+        v = O.normal_f16((B, self.Hkv, self.D), seed + 1)
+        q = O.normal_f16((B, self.Hq, self.D), seed + 2)
+        kd, vd, qd = to_dev(k), to_dev(v), to_dev(q)
+        od = torch.full((B, self.Hq, self.D), 0x7e00, dtype=torch.int16, device="cuda")  # NaN fill
+        sc = scale if scale is not None else 1.0 / math.sqrt(self.D)
+        self.cache.attention_step(layer, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(),
+                                  sids, sc)
+        self.cache.sync_check()
+        got = O.f16_to_f32(from_dev(od))
+        for i, sid in enumerate(sids):
+            pos = self.cache.get_seq_len(sid)
+            self._record(sid, layer, pos, k[i:i + 1], v[i:i + 1])
+            qi = O.rope_row(q[i], self.cos, self.sin, pos) if self.rope else q[i]
+            kk = np.stack(self.logical_k[(sid, layer)])
+            vv = np.stack(self.logical_v[(sid, layer)])
+            ref = O.decode_one(qi, kk, vv, sc)
+            check_close(got[i], ref, f"attention step layer {layer} seq {sid} pos {pos}")
+
     def check_pool_bit_exact(self):
         """Gathers every sequence back from the device pool via its block
         table and compares bit-for-bit with the oracle's logical K/V."""

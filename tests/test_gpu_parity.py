@@ -61,6 +61,29 @@ def test_decode_shapes(D, G, bs):
     r.decode_and_check(0, sids, seed=77)
 
 
+@pytest.mark.parametrize("D,G,rope", [(128, 4, True), (64, 8, True), (256, 1, True), (128, 8, False)])
+def test_attention_step_engine_flow(D, G, rope):
+    """The decode branch of TransformerLayer::attention for a batch, layer by
+    layer (per-layer append of the new token, then decode with RoPE on Q at
+    the same position), over several steps of ragged sequences; the pool
+    stays bit-exact."""
+    Hkv = 2
+    r = Run.create(L=2, Hq=Hkv * G, Hkv=Hkv, D=D, bs=16, max_seq_len=600, max_batch=6, rope=rope,
+                   permute_seed=11)
+    lens = [1, 15, 16, 47, 300, 511]
+    sids = [r.allocate(600) for _ in lens]
+    for i, (sid, S) in enumerate(zip(sids, lens)):
+        r.prefill(sid, S, seed=400 + i)
+    for step in range(4):
+        for layer in range(2):
+            r.attention_step_and_check(layer, sids, seed=7000 + 10 * step + 3 * layer)
+        for sid in sids:
+            r.cache.advance_seq_len(sid, 1)
+    r.check_pool_bit_exact()
+    for sid, S in zip(sids, lens):
+        assert r.cache.get_seq_len(sid) == S + 4
+
+
 def test_single_long_sequence_many_splits():
     """One KV head, one long sequence: every worker gets a slice of the same
     unit, so the merge pass combines hundreds of partials."""

@@ -153,6 +153,28 @@ def test_append_on_bookkeeping_backend_refuses_compute():
     assert c.get_seq_len(sid) == 0
 
 
+def test_attention_step_validates_then_refuses_compute():
+    """tl_attention_step: argument errors as appendKV / decodeAttention report
+    them; on the bookkeeping backend it refuses before touching any state."""
+    c = make(2, 4, 64, 32, 2)
+    sid = c.allocate_sequence(16)
+    with pytest.raises(T.InvalidArgument) as e:
+        c.attention_step(2, 16, 16, 16, 16, [sid])
+    assert "Invalid layer_idx" in str(e.value)
+    with pytest.raises(T.InvalidArgument) as e:
+        c.attention_step(0, None, 16, 16, 16, [sid])
+    assert "query is null" in str(e.value)
+    with pytest.raises(T.NotFound):
+        c.attention_step(0, 16, 16, 16, 16, [sid + 99])
+    with pytest.raises(T.InvalidArgument) as e:
+        c.attention_step(0, 16, 16, 16, 16, [sid, sid])
+    assert "duplicate" in str(e.value)
+    with pytest.raises(T.NoDevice):
+        c.attention_step(0, 16, 16, 16, 16, [sid])
+    assert c.get_seq_len(sid) == 0
+    assert c.pool_stats().used_blocks == 1  # the block taken at allocation, nothing grown
+
+
 def test_advance_clamps_to_capacity():  # :262-273
     c = make(2, 4, 8, 32, 2)
     sid = c.allocate_sequence(5)

@@ -106,6 +106,12 @@ struct DecodeArgs {
     int layer;
     int group;              // G = Hq / Hkv
     float scale_log2;       // softmax scale * log2(e)
+    // Non-null: Q is rotated by this RoPE table ([rope_max_pos][D/2] fp32) at
+    // each sequence's newest position (len - 1) before use, rounded as the
+    // append kernel rounds K.
+    const float *rope_cos;
+    const float *rope_sin;
+    int rope_max_pos;
     int nseq;
     long long total_items;  // W
     int workers;            // V

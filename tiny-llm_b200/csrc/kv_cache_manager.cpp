@@ -87,6 +87,13 @@ Result<void> KVCacheManager::decodeAttention(int layer_idx, const half *q, half 
                                       scale, stream));
 }
 
+Result<void> KVCacheManager::attentionStep(int layer_idx, const half *q, const half *k_new,
+                                           const half *v_new, half *out, const std::vector<int> &seq_ids,
+                                           float scale, cudaStream_t stream) {
+    return status(tl_attention_step(h_, layer_idx, q, k_new, v_new, out, seq_ids.data(),
+                                    (int)seq_ids.size(), scale, stream));
+}
+
 Result<std::vector<int>> KVCacheManager::getBlockTable(int seq_id) const {
     int n = 0;
     if (tl_get_block_table(h_, seq_id, nullptr, 0, &n) != TL_OK)

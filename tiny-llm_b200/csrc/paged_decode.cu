@@ -214,6 +214,39 @@ __device__ void pull_peer_slices(const DecodeArgs &a) {
     }
 }
 
+// Rotates a lane's Q fragments by the RoPE table at position pos (rotate-half:
+// element d pairs with d + D/2, which sits in k-step ks + D/32 of the same
+// lane). Each product and sum is rounded separately (__fmul_rn, __fsub_rn,
+// __fadd_rn) and the result converted to fp16 with round-to-nearest-even,
+// the append kernel's sequence for K.
+template <int D>
+__device__ __forceinline__ void rope_q(uint32_t (&qf)[D / 16][2], const DecodeArgs &a, int pos, int tig) {
+    constexpr int kKS = D / 16, kHalfD = D / 2;
+    if (pos < 0 || pos >= a.rope_max_pos) {
+        atomicOr(a.g.err, kErrPosRange);
+        return;
+    }
+    const float *ct = a.rope_cos + (long long)pos * kHalfD;
+    const float *st = a.rope_sin + (long long)pos * kHalfD;
+#pragma unroll
+    for (int ks = 0; ks < kKS / 2; ++ks) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int d = ks * 16 + j * 8 + 2 * tig;  // and d + 1, both < D/2
+            const float2 c = *reinterpret_cast<const float2 *>(ct + d);
+            const float2 sn = *reinterpret_cast<const float2 *>(st + d);
+            const float2 x1 = __half22float2(*reinterpret_cast<const __half2 *>(&qf[ks][j]));
+            const float2 x2 = __half22float2(*reinterpret_cast<const __half2 *>(&qf[ks + kKS / 2][j]));
+            const __half2 r1 = __halves2half2(__float2half_rn(__fsub_rn(__fmul_rn(x1.x, c.x), __fmul_rn(x2.x, sn.x))),
+                                              __float2half_rn(__fsub_rn(__fmul_rn(x1.y, c.y), __fmul_rn(x2.y, sn.y))));
+            const __half2 r2 = __halves2half2(__float2half_rn(__fadd_rn(__fmul_rn(x2.x, c.x), __fmul_rn(x1.x, sn.x))),
+                                              __float2half_rn(__fadd_rn(__fmul_rn(x2.y, c.y), __fmul_rn(x1.y, sn.y))));
+            qf[ks][j] = *reinterpret_cast<const uint32_t *>(&r1);
+            qf[ks + kKS / 2][j] = *reinterpret_cast<const uint32_t *>(&r2);
+        }
+    }
+}
+
 // Maps a flat item index to (sequence, kv_head, tile). prefix[] lives in the
 // kernel's parameter space; the search is uniform across the warp.
 __device__ __forceinline__ ItemPos locate(const DecodeArgs &a, long long w) {
@@ -577,6 +610,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
                     qf[ks][1] = 0u;
                 }
             }
+            if (a.rope_cos != nullptr && gid < G) rope_q<D>(qf, a, a.len[p.b] - 1, tig);
 #pragma unroll
             for (int dm = 0; dm < C::kKS; ++dm) acc[dm][0] = acc[dm][1] = acc[dm][2] = acc[dm][3] = 0.f;
             m0 = m1 = -INFINITY;

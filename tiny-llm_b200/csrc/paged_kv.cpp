@@ -281,6 +281,56 @@ int launch_rows(tl_cache *c, const std::vector<int> &row_block, const std::vecto
     return TL_OK;
 }
 
+// One new token per sequence (at its current length) for layers
+// [layer0, layer0 + num_layers): k/v are [num_layers][num_seqs][Hkv][D].
+// Validates every sequence first; block growth is rolled back on failure.
+int append_token_rows(tl_cache *c, const char *ctx, const int *seq_ids, int num_seqs, const void *k,
+                      const void *v, int layer0, int num_layers, cudaStream_t stream) {
+    if (num_seqs < 0) return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": num_seqs must be >= 0");
+    if (num_seqs == 0) return TL_OK;
+    if (!seq_ids) return set_error(c, TL_ERR_INVALID_ARG, "seq_ids is null");
+    if (!k) return set_error(c, TL_ERR_INVALID_ARG, "new_k is null");
+    if (!v) return set_error(c, TL_ERR_INVALID_ARG, "new_v is null");
+    std::vector<Sequence *> ss((size_t)num_seqs);
+    std::unordered_set<int> seen;
+    for (int i = 0; i < num_seqs; ++i) {
+        Sequence *s = find_seq(c, seq_ids[i]);
+        if (!s)
+            return set_error(c, TL_ERR_NOT_FOUND,
+                             std::string(ctx) + ": sequence not found: " + std::to_string(seq_ids[i]));
+        if (!seen.insert(seq_ids[i]).second)
+            return set_error(c, TL_ERR_INVALID_ARG,
+                             std::string(ctx) + ": duplicate sequence id " + std::to_string(seq_ids[i]));
+        if (s->len + 1 > s->max_len)
+            return set_error(c, TL_ERR_OVERFLOW,
+                             std::string(ctx) + ": cache overflow. seq " + std::to_string(seq_ids[i]) +
+                                 " Current: " + std::to_string(s->len) +
+                                 ", appending: 1, max: " + std::to_string(s->max_len));
+        ss[(size_t)i] = s;
+    }
+    if (!c->on_device)
+        return set_error(c, TL_ERR_NO_DEVICE, std::string(ctx) + ": handle has no CUDA device (bookkeeping backend)");
+    DeviceGuard guard(c);
+    std::vector<std::pair<Sequence *, int>> undo;
+    size_t mark = c->pending.size();
+    std::vector<int> rb((size_t)num_seqs), rp((size_t)num_seqs);
+    for (int i = 0; i < num_seqs; ++i) {
+        Sequence &s = *ss[(size_t)i];
+        int st = ensure_blocks(c, s, (long long)s.len + 1, mark, &undo);
+        if (st != TL_OK) {
+            rollback(c, mark, undo);
+            return st;
+        }
+        rp[(size_t)i] = s.len;
+        rb[(size_t)i] = s.blocks[(size_t)(s.len / c->bs)];
+    }
+    const long long row = (long long)c->cfg.num_kv_heads * c->cfg.head_dim;
+    int st = launch_rows(c, rb, rp, k, v, layer0, num_layers, row * num_seqs, row, stream);
+    if (st != TL_OK) return st;
+    for (Sequence *s : ss) s->written = std::max(s->written, s->len + 1);
+    return TL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -640,50 +690,8 @@ int tl_append_kv(tl_cache *c, int seq_id, int layer, const void *k, const void *
 int tl_append_kv_all_layers(tl_cache *c, const int *seq_ids, int num_seqs, const void *k,
                             const void *v, tl_stream_t stream) {
     if (!c) return TL_ERR_INVALID_ARG;
-    if (num_seqs < 0) return set_error(c, TL_ERR_INVALID_ARG, "appendKVAllLayers: num_seqs must be >= 0");
-    if (num_seqs == 0) return TL_OK;
-    if (!seq_ids) return set_error(c, TL_ERR_INVALID_ARG, "seq_ids is null");
-    if (!k) return set_error(c, TL_ERR_INVALID_ARG, "new_k is null");
-    if (!v) return set_error(c, TL_ERR_INVALID_ARG, "new_v is null");
-    std::vector<Sequence *> ss((size_t)num_seqs);
-    std::unordered_set<int> seen;
-    for (int i = 0; i < num_seqs; ++i) {
-        Sequence *s = find_seq(c, seq_ids[i]);
-        if (!s)
-            return set_error(c, TL_ERR_NOT_FOUND,
-                             "appendKVAllLayers: sequence not found: " + std::to_string(seq_ids[i]));
-        if (!seen.insert(seq_ids[i]).second)
-            return set_error(c, TL_ERR_INVALID_ARG,
-                             "appendKVAllLayers: duplicate sequence id " + std::to_string(seq_ids[i]));
-        if (s->len + 1 > s->max_len)
-            return set_error(c, TL_ERR_OVERFLOW,
-                             "appendKVAllLayers: cache overflow. seq " + std::to_string(seq_ids[i]) +
-                                 " Current: " + std::to_string(s->len) +
-                                 ", appending: 1, max: " + std::to_string(s->max_len));
-        ss[(size_t)i] = s;
-    }
-    if (!c->on_device)
-        return set_error(c, TL_ERR_NO_DEVICE, "appendKVAllLayers: handle has no CUDA device (bookkeeping backend)");
-    DeviceGuard guard(c);
-    std::vector<std::pair<Sequence *, int>> undo;
-    size_t mark = c->pending.size();
-    std::vector<int> rb((size_t)num_seqs), rp((size_t)num_seqs);
-    for (int i = 0; i < num_seqs; ++i) {
-        Sequence &s = *ss[(size_t)i];
-        int st = ensure_blocks(c, s, (long long)s.len + 1, mark, &undo);
-        if (st != TL_OK) {
-            rollback(c, mark, undo);
-            return st;
-        }
-        rp[(size_t)i] = s.len;
-        rb[(size_t)i] = s.blocks[(size_t)(s.len / c->bs)];
-    }
-    const long long row = (long long)c->cfg.num_kv_heads * c->cfg.head_dim;
-    int st = launch_rows(c, rb, rp, k, v, 0, c->cfg.num_layers, row * num_seqs, row,
-                         (cudaStream_t)stream);
-    if (st != TL_OK) return st;
-    for (Sequence *s : ss) s->written = std::max(s->written, s->len + 1);
-    return TL_OK;
+    return append_token_rows(c, "appendKVAllLayers", seq_ids, num_seqs, k, v, 0, c->cfg.num_layers,
+                             (cudaStream_t)stream);
 }
 
 // advanceSeqLen (reference src/kv_cache.cpp:240-259): clamps to max_len.
@@ -782,7 +790,7 @@ struct PeerSpec {
 
 int decode_impl(tl_cache *c, const char *ctx, int layer, const void *q, void *o,
                 const int *seq_ids, int num_seqs, float scale, cudaStream_t stream,
-                const PeerSpec *peer) {
+                const PeerSpec *peer, bool rope_q = false) {
     if (layer < 0 || layer >= c->cfg.num_layers)
         return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, ctx, layer));
     if (num_seqs < 0) return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": num_seqs must be >= 0");
@@ -838,6 +846,11 @@ int decode_impl(tl_cache *c, const char *ctx, int layer, const void *q, void *o,
         a.layer = layer;
         a.group = c->group;
         a.scale_log2 = scale * 1.4426950408889634f;
+        if (rope_q) {
+            a.rope_cos = c->rope_cos;
+            a.rope_sin = c->rope_sin;
+            a.rope_max_pos = c->cfg.max_seq_len;
+        }
         a.nseq = n;
         if (peer) {  // write this rank's slice locally, publish, pull the others
             const size_t slice = (size_t)n * (size_t)row * 2;
@@ -912,6 +925,25 @@ int tl_decode_attention(tl_cache *c, int layer, const void *q, void *o, const in
     if (!c) return TL_ERR_INVALID_ARG;
     return decode_impl(c, "decodeAttention", layer, q, o, seq_ids, num_seqs, scale,
                        (cudaStream_t)stream, nullptr);
+}
+
+// The decode branch of TransformerLayer::attention (reference
+// src/transformer.cpp:222-237) for a batch: appendKV of each sequence's new
+// token at its current length, then attention over len + 1 tokens, with Q
+// rotated by the handle's RoPE table at that position when K is rotated on
+// append.
+int tl_attention_step(tl_cache *c, int layer, const void *q, const void *k_new, const void *v_new,
+                      void *o, const int *seq_ids, int num_seqs, float scale, tl_stream_t stream) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= c->cfg.num_layers)
+        return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, "attentionStep", layer));
+    if (num_seqs > 0 && (!q || !o))
+        return set_error(c, TL_ERR_INVALID_ARG, !q ? "query is null" : "output is null");
+    int st = append_token_rows(c, "attentionStep", seq_ids, num_seqs, k_new, v_new, layer, 1,
+                               (cudaStream_t)stream);
+    if (st != TL_OK) return st;
+    return decode_impl(c, "attentionStep", layer, q, o, seq_ids, num_seqs, scale, (cudaStream_t)stream,
+                       nullptr, c->cfg.rope_on_append != 0);
 }
 
 int tl_peer_init(tl_cache *c, int rank, int world, size_t gather_bytes, void *ipc_handle) {

@@ -43,7 +43,7 @@ EXPORTED_SYMBOLS = [
     "tl_get_pool", "tl_decode_attention", "tl_sync_check", "tl_rope_table",
     "tl_permute_free_blocks", "tl_debug_inject_alloc_failure", "tl_version",
     "tl_decode_attention_static", "tl_peer_init", "tl_peer_connect", "tl_peer_buffer",
-    "tl_decode_attention_peer",
+    "tl_decode_attention_peer", "tl_attention_step",
 ]
 
 
@@ -140,6 +140,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_get_pool_stats": (i, [vp, C.POINTER(PoolStats)]),
         "tl_get_pool": (i, [vp, C.POINTER(vp), C.POINTER(sz)]),
         "tl_decode_attention": (i, [vp, i, vp, vp, ip, i, f, vp]),
+        "tl_attention_step": (i, [vp, i, vp, vp, vp, vp, ip, i, f, vp]),
         "tl_sync_check": (i, [vp, vp]),
         "tl_rope_table": (None, [C.POINTER(C.c_float), C.POINTER(C.c_float), i, i, f]),
         "tl_permute_free_blocks": (i, [vp, C.c_ulonglong]),
@@ -292,6 +293,13 @@ class KVCache:
     def decode_attention(self, layer, q_ptr, o_ptr, seq_ids, scale=0.0, stream=0):
         self._check(self._lib.tl_decode_attention(self._h, int(layer), q_ptr, o_ptr, _ids(seq_ids),
                                                   len(seq_ids), float(scale), stream or None))
+
+    def attention_step(self, layer, q_ptr, k_ptr, v_ptr, o_ptr, seq_ids, scale=0.0, stream=0):
+        """Appends one token per sequence in `layer`, then decodes (Q rotated
+        like K when the cache rotates on append); advance afterwards."""
+        self._check(self._lib.tl_attention_step(self._h, int(layer), q_ptr, k_ptr, v_ptr, o_ptr,
+                                                _ids(seq_ids), len(seq_ids), float(scale),
+                                                stream or None))
 
     # -- head-sharded peer gather (one process per GPU) ----------------------
     def peer_init(self, rank: int, world: int, gather_bytes: int) -> bytes:
