@@ -13,7 +13,6 @@
 #include <cuda_fp16.h>
 
 #include "kernels.h"
-#include "ptx.cuh"
 
 namespace tllm {
 namespace {
@@ -58,11 +57,6 @@ __device__ __forceinline__ void rope8(const uint4 &x1v, const uint4 &x2v, const 
 }
 
 __global__ void __launch_bounds__(128) append_kernel(const __grid_constant__ AppendArgs a) {
-    // Programmatic dependent launch: the next kernel (typically a decode of
-    // the same layer) may begin launching now; this kernel touches no global
-    // memory before the previous grid has completed.
-    ptx::griddep_launch_dependents();
-    ptx::griddep_wait();
     const PoolGeom &g = a.g;
     const int row = blockIdx.x;
     const int lyr = blockIdx.y;
@@ -150,38 +144,23 @@ __global__ void __launch_bounds__(128) append_kernel(const __grid_constant__ App
 }
 
 __global__ void apply_deltas_kernel(const __grid_constant__ DeltaArgs a) {
-    ptx::griddep_launch_dependents();
-    ptx::griddep_wait();
     for (int i = threadIdx.x; i < a.ndeltas; i += blockDim.x)
         a.block_tables[(long long)a.delta_slot[i] * a.bt_stride + a.delta_idx[i]] = a.delta_block[i];
 }
 
 }  // namespace
 
-// Both launches allow programmatic stream serialization: they may start
-// while the previous kernel drains, and wait for it before any access.
-template <typename Args>
-cudaError_t launch_pdl(void (*kernel)(Args), dim3 grid, const Args &a, cudaStream_t s) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(128);
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, a);
-}
-
 cudaError_t launch_append(const AppendArgs &a, cudaStream_t s) {
     if (a.nrows <= 0 || a.num_layers <= 0) return cudaSuccess;
-    return launch_pdl(append_kernel, dim3(a.nrows, a.num_layers), a, s);
+    dim3 grid(a.nrows, a.num_layers);
+    append_kernel<<<grid, 128, 0, s>>>(a);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_apply_deltas(const DeltaArgs &a, cudaStream_t s) {
     if (a.ndeltas <= 0) return cudaSuccess;
-    return launch_pdl(apply_deltas_kernel, dim3(1), a, s);
+    apply_deltas_kernel<<<1, 128, 0, s>>>(a);
+    return cudaGetLastError();
 }
 
 }  // namespace tllm
