@@ -61,15 +61,18 @@ def test_decode_shapes(D, G, bs):
     r.decode_and_check(0, sids, seed=77)
 
 
-@pytest.mark.parametrize("D,G,rope", [(128, 4, True), (64, 8, True), (256, 1, True), (128, 8, False)])
-def test_attention_step_engine_flow(D, G, rope):
+@pytest.mark.parametrize("D,G,rope,bs", [(128, 4, True, 16), (64, 8, True, 32), (256, 1, True, 16),
+                                         (128, 8, False, 32)])
+def test_attention_step_engine_flow(D, G, rope, bs):
     """The decode branch of TransformerLayer::attention for a batch, layer by
     layer (per-layer append of the new token, then decode with RoPE on Q at
     the same position), over several steps of ragged sequences; the pool
     stays bit-exact."""
     Hkv = 2
-    r = Run.create(L=2, Hq=Hkv * G, Hkv=Hkv, D=D, bs=16, max_seq_len=600, max_batch=6, rope=rope,
+    r = Run.create(L=2, Hq=Hkv * G, Hkv=Hkv, D=D, bs=bs, max_seq_len=600, max_batch=6, rope=rope,
                    permute_seed=11)
+    # new tokens land mid-tile, at the start of a tile (built without a load)
+    # and at the start of a block (a block the kernel enters in the table)
     lens = [1, 15, 16, 47, 300, 511]
     sids = [r.allocate(600) for _ in lens]
     for i, (sid, S) in enumerate(zip(sids, lens)):
@@ -82,6 +85,29 @@ def test_attention_step_engine_flow(D, G, rope):
     r.check_pool_bit_exact()
     for sid, S in zip(sids, lens):
         assert r.cache.get_seq_len(sid) == S + 4
+
+
+def test_attention_step_overwrites_pending_token_and_refuses_unadvanced_runs():
+    """One token appended at the current length and not advanced is
+    overwritten by the step (same position); a multi-token run appended past
+    the length and not advanced is refused before any state changes."""
+    r = Run.create(L=1, Hq=8, Hkv=2, D=128, bs=16, max_seq_len=200, max_batch=2, rope=True)
+    sids = [r.allocate(200) for _ in range(2)]
+    for i, sid in enumerate(sids):
+        r.prefill(sid, 40 + i, seed=800 + i)
+    r.step_append(sids, seed=810)                  # position len, pending
+    r.attention_step_and_check(0, sids, seed=820)  # the same position again
+    r.check_pool_bit_exact()
+    for sid in sids:
+        r.cache.advance_seq_len(sid, 1)
+    k = O.normal_f16((2, r.Hkv, r.D), 830)
+    kd = to_dev(k)
+    r.cache.append_kv(sids[0], 0, kd.data_ptr(), kd.data_ptr(), 2)  # two pending tokens
+    used = r.cache.pool_stats().used_blocks
+    with pytest.raises(T.InvalidArgument) as e:
+        r.cache.attention_step(0, kd.data_ptr(), kd.data_ptr(), kd.data_ptr(), kd.data_ptr(), sids)
+    assert "advance it first" in str(e.value)
+    assert r.cache.pool_stats().used_blocks == used
 
 
 def test_single_long_sequence_many_splits():

@@ -939,6 +939,19 @@ int tl_attention_step(tl_cache *c, int layer, const void *q, const void *k_new, 
         return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, "attentionStep", layer));
     if (num_seqs > 0 && (!q || !o))
         return set_error(c, TL_ERR_INVALID_ARG, !q ? "query is null" : "output is null");
+    if (c->on_device && !decode_geometry_supported(c))
+        return set_error(c, TL_ERR_UNSUPPORTED,
+                         "attentionStep: supported shapes are head_dim 64/128/256, block_size 16/32, "
+                         "query group 1..8");
+    // The new token is each sequence's newest attended one (Q's position):
+    // tokens appended past the length and not yet advanced are refused.
+    for (int i = 0; i < num_seqs && seq_ids; ++i) {
+        const Sequence *s = find_seq(c, seq_ids[i]);
+        if (s && s->written > s->len + 1)
+            return set_error(c, TL_ERR_INVALID_ARG,
+                             "attentionStep: sequence " + std::to_string(seq_ids[i]) +
+                                 " has tokens appended past its length; advance it first");
+    }
     int st = append_token_rows(c, "attentionStep", seq_ids, num_seqs, k_new, v_new, layer, 1,
                                (cudaStream_t)stream);
     if (st != TL_OK) return st;
