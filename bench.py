@@ -67,6 +67,10 @@ CONFIGS = {
     "c5s": dict(workload="c5 steady-state batch, static: 225 seqs, log-U[32,4096] prompts",
                 L=32, Hq=32, Hkv=8, D=128, bs=16, lens="loguniform", B=225, lo=32, hi=4096,
                 rope=True, permute=True),
+    # Paged prefill (the prompt side of the engine): 8 fresh 4096-token
+    # prompts, Llama-3-8B GQA shape; 4 layers (every layer is the same work).
+    "pf": dict(workload="prefill: 8 prompts x 4096 tokens, Llama-3-8B GQA, 4 layers",
+               L=4, Hq=32, Hkv=8, D=128, bs=16, lens=[4096] * 8, rope=True),
     "c5": dict(workload="c5 8B GQA continuous-batching churn: Poisson(4) arrivals, prompts "
                         "log-U[32,4096], geometric(256) generations, <=256 active, pool ~80% occupied",
                L=32, Hq=32, Hkv=8, D=128, bs=16, lens="churn", rope=True, permute=True),
@@ -492,6 +496,95 @@ def run_churn(cfg, args, world, rank, local):
     return res
 
 
+# -------------------------------------------------------- prefill (pf) ----
+
+def run_prefill(cfg, args, world, rank, local):
+    """A step = every prompt's K/V appended to every layer (tl_append_kv) and
+    the causal prefill attention of every layer (tl_prefill_attention) over
+    fresh sequences, which are released afterwards. value = causal attention
+    FLOPs (4 * Hq * D per (query, key) pair with key <= query) per second."""
+    import torch
+    import tiny_llm_b200 as T
+    L, Hq, Hkv, D, bs = cfg["L"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["bs"]
+    lens = list(cfg["lens"])
+    B, n = len(lens), max(lens)
+    cache = T.KVCache(num_layers=L, num_kv_heads=Hkv, head_dim=D, max_seq_len=n, max_batch_size=B,
+                      block_size=bs, num_q_heads=Hq, rope_on_append=cfg["rope"], rope_theta=10000.0,
+                      device=local)
+    cache.permute_free_blocks(args.seed + rank)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 7919 + rank)
+    k = torch.randn((L, B, n, Hkv, D), dtype=torch.float16, device="cuda", generator=gen)
+    v = torch.randn((L, B, n, Hkv, D), dtype=torch.float16, device="cuda", generator=gen)
+    q = torch.randn((L, B * n, Hq, D), dtype=torch.float16, device="cuda", generator=gen)
+    o = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(D)
+    flops = L * B * 4 * Hq * D * (n * (n + 1) // 2)
+    pairs = [None]
+
+    def step(events=None):
+        sids = [cache.allocate_sequence(n) for _ in range(B)]
+        for l in range(L):
+            for b, sid in enumerate(sids):
+                cache.append_kv(sid, l, k[l, b].data_ptr(), v[l, b].data_ptr(), n, sp)
+            if events is not None:
+                events[l][0].record(stream)
+            cache.prefill_attention(l, q[l].data_ptr(), o[l].data_ptr(), sids, [n] * B, scale, sp)
+            if events is not None:
+                events[l][1].record(stream)
+        for sid in sids:
+            cache.release_sequence(sid)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
+    launches0 = cache.pool_stats().kernel_launches
+    a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    z.record(stream)
+    z.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(z)
+    launches = cache.pool_stats().kernel_launches - launches0
+    cache.sync_check(sp)
+    # roofline pass: events around each layer's prefill launch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    step(evs)
+    torch.cuda.synchronize()
+    pf_ms = sum(x.elapsed_time(y) for x, y in evs)
+    # e2e: each step's Q/K/V from pinned host memory, outputs back to the host
+    hq = torch.empty(q.shape, dtype=torch.float16, pin_memory=True)
+    hk = torch.empty(k.shape, dtype=torch.float16, pin_memory=True)
+    hv = torch.empty(v.shape, dtype=torch.float16, pin_memory=True)
+    ho = torch.empty(o.shape, dtype=torch.float16, pin_memory=True)
+    hq.copy_(q.cpu()); hk.copy_(k.cpu()); hv.copy_(v.cpu())
+    torch.cuda.synchronize()
+    barrier(world)
+    ea, ez = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for _ in range(args.steps):
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        step()
+        ho.copy_(o, non_blocking=True)
+    ez.record(stream)
+    ez.synchronize()
+    e2e_ms = ea.elapsed_time(ez)
+    cache.sync_check(sp)
+    cache.close()
+    return dict(ms=ms, flops=flops * args.steps, pf_ms=pf_ms, pf_flops=flops, e2e_ms=e2e_ms,
+                h2d=(hq.numel() + hk.numel() + hv.numel()) * 2, d2h=ho.numel() * 2,
+                launches=launches, clocks=clocks, B=B, n=n)
+
+
 # ---------------------------------------------------------- reference path --
 
 def load_ref():
@@ -724,6 +817,9 @@ def main():
         if args.config == "c5":
             res, why = None, ("reference arm runs uniform-length configs only; the reference "
                               "engine has no continuous batching (max_batch_size=1)")
+        elif args.config == "pf":
+            res, why = None, ("reference arm covers the decode configs; the reference prefill kernel "
+                              "is compared in tests/test_gpu_reference.py")
         else:
             res, why = run_reference(cfg, args, world, rank, local)
         if res is None:
@@ -755,6 +851,39 @@ def main():
                             "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
                     "decode_kernel_gbs": round(kv / world / (res["dec_ms"] / 1e3) / 1e9, 1) if res["dec_ms"] else None,
                     "clocks": res["clocks"]}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    if args.config == "pf":
+        res = run_prefill(cfg, args, world, rank, local)
+        ms = barrier_max(res["ms"], world)
+        fl = barrier_sum(res["flops"], world)
+        e2e_ms = barrier_max(res["e2e_ms"], world)
+        if rank == 0:
+            pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+            tpeak = float(pk.get("bf16_tflops", 1590.0))
+            achieved = res["pf_flops"] / (res["pf_ms"] / 1e3) / 1e12
+            line = {"metric": "prefill attention TFLOP/s (causal)", "value": round(fl / (ms / 1e3) / 1e12, 2),
+                    "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+                    "data": "synthetic N(0,1) fp16 Q/K/V from a seeded generator (no dataset)",
+                    "config": dict({k: v for k, v in base_config.items() if k not in ("l2", "flow")},
+                                   global_batch=res["B"] * world, seq_len=res["n"],
+                                   step="append every layer's prompt K/V, causal prefill per layer, release",
+                                   l2="K/V of a layer (67 MB) kept in L2 across the query blocks; Q/O stream"),
+                    "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak,
+                                 "unit": "TFLOP/s", "frac": round(achieved / tpeak, 4), "traffic": None,
+                                 "kernel": "paged_prefill_kernel (mma.sync m16n8k16)",
+                                 "peak_source": "measured cuBLAS bf16 dense (MEASURED_PEAKS.json bf16_tflops)"
+                                 if pk else "fallback"},
+                    "cpu_baseline": None,
+                    "e2e": {"value": round(fl / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                            "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
+                    "clocks": res["clocks"], "gpu_launches": res["launches"]}
             print(json.dumps(line), flush=True)
         if world > 1:
             import torch.distributed as dist

@@ -87,6 +87,11 @@ class KVCacheManager {
     Result<void> attentionStep(int layer_idx, const half *q, const half *k_new, const half *v_new,
                                half *out, const std::vector<int> &seq_ids, float scale = 0.0f,
                                cudaStream_t stream = 0);
+    // Replacement of kernels::attention_prefill: causal attention of each
+    // sequence's last num_tokens[i] written tokens over the paged cache.
+    Result<void> prefillAttention(int layer_idx, const half *q, half *out, const std::vector<int> &seq_ids,
+                                  const std::vector<int> &num_tokens, float scale = 0.0f,
+                                  cudaStream_t stream = 0);
     Result<std::vector<int>> getBlockTable(int seq_id) const;
     tl_pool_stats getPoolStats() const noexcept;
     Result<void> syncCheck(cudaStream_t stream = 0);

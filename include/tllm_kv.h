@@ -187,6 +187,18 @@ int tl_decode_attention(tl_cache *cache, int layer, const void *q, void *o, cons
 int tl_attention_step(tl_cache *cache, int layer, const void *q, const void *k_new, const void *v_new,
                       void *o, const int *seq_ids, int num_seqs, float scale, tl_stream_t stream);
 
+/* Causal prefill attention over the paged cache, replacing
+ * kernels::attention_prefill (reference kernels/attention.cu:131-237, called
+ * at src/transformer.cpp:238-242 over the prompt's own buffers): after the
+ * prompt's K/V are appended (tl_append_kv, any number of tokens), sequence
+ * i's num_tokens[i] query rows are its last num_tokens[i] written tokens;
+ * each attends the sequence's tokens up to its own position (so a prompt
+ * that continues a cached prefix sees the prefix), with Q rotated at its
+ * position when K is rotated on append. q/o: [sum(num_tokens)][Hq][D] fp16,
+ * sequence after sequence. head_dim 64 or 128. */
+int tl_prefill_attention(tl_cache *cache, int layer, const void *q, void *o, const int *seq_ids,
+                         const int *num_tokens, int num_seqs, float scale, tl_stream_t stream);
+
 /* ---- Head-sharded decode across the GPUs of one node -------------------
  * No reference counterpart (the reference is single-GPU). With KV heads
  * split over `world` ranks (one process per GPU), each rank's decode writes

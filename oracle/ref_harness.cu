@@ -99,4 +99,20 @@ int ref_attention_decode(const void *q, const void *k, const void *v, void *o, f
     return 0;
 }
 
+// kernels::attention_prefill (kernels/attention.cu:131-237) followed by the
+// launch check the reference omits; q/k/v/o are [batch][heads][seq][dim].
+int ref_attention_prefill(const void *q, const void *k, const void *v, void *o, float scale,
+                          int batch, int heads, int seq_len, int head_dim, void *stream) {
+    tiny_llm::kernels::attention_prefill(static_cast<const half *>(q), static_cast<const half *>(k),
+                                         static_cast<const half *>(v), static_cast<half *>(o), scale,
+                                         batch, heads, seq_len, head_dim,
+                                         static_cast<cudaStream_t>(stream));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        g_err = cudaGetErrorString(e);
+        return (int)e;
+    }
+    return 0;
+}
+
 }  // extern "C"

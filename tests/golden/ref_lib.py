@@ -38,6 +38,7 @@ def load():
         lib.ref_kv_get_cache.argtypes = [vp, i, i, C.POINTER(vp), C.POINTER(vp)]
         lib.ref_kv_destroy.argtypes = [vp]
         lib.ref_attention_decode.argtypes = [vp, vp, vp, vp, f, i, i, i, i, vp]
+        lib.ref_attention_prefill.argtypes = [vp, vp, vp, vp, f, i, i, i, i, vp]
         lib.ref_last_error.restype = C.c_char_p
         _lib = lib
     return _lib
@@ -48,6 +49,13 @@ def attention_decode(q_dev, k_dev, v_dev, o_dev, scale, B, H, S, D):
     rc = load().ref_attention_decode(q_dev, k_dev, v_dev, o_dev, scale, B, H, S, D, None)
     if rc != 0:
         raise RuntimeError("reference attention_decode failed: " + load().ref_last_error().decode())
+
+
+def attention_prefill(q_dev, k_dev, v_dev, o_dev, scale, B, H, S, D):
+    """kernels::attention_prefill on [B][H][S][D] Q/K/V/O (device pointers)."""
+    rc = load().ref_attention_prefill(q_dev, k_dev, v_dev, o_dev, scale, B, H, S, D, None)
+    if rc != 0:
+        raise RuntimeError("reference attention_prefill failed: " + load().ref_last_error().decode())
 
 
 class RefCache:

@@ -110,6 +110,57 @@ def test_attention_step_overwrites_pending_token_and_refuses_unadvanced_runs():
     assert r.cache.pool_stats().used_blocks == used
 
 
+def _prefill_and_check(r, sids, prefixes, ntoks, seed):
+    """Appends ntoks[i] prompt tokens after a cached prefix of prefixes[i]
+    tokens, runs the paged prefill over them and checks every query row
+    against the oracle: the fp64 decode restatement over the tokens up to
+    the row's position (Q rotated at that position when K is)."""
+    import torch
+    for i, (sid, P0, n) in enumerate(zip(sids, prefixes, ntoks)):
+        if P0:
+            r.prefill(sid, P0, seed=seed + 10 * i)  # appended and advanced
+        k = O.normal_f16((n, r.Hkv, r.D), seed + 10 * i + 1)
+        v = O.normal_f16((n, r.Hkv, r.D), seed + 10 * i + 2)
+        kd, vd = to_dev(k), to_dev(v)
+        r.cache.append_kv(sid, 0, kd.data_ptr(), vd.data_ptr(), n)
+        r._record(sid, 0, P0, k, v)
+    rows = sum(ntoks)
+    q = O.normal_f16((rows, r.Hq, r.D), seed + 999)
+    qd = to_dev(q)
+    od = torch.full((rows, r.Hq, r.D), 0x7e00, dtype=torch.int16, device="cuda")  # NaN fill
+    sc = 1.0 / math.sqrt(r.D)
+    r.cache.prefill_attention(0, qd.data_ptr(), od.data_ptr(), sids, ntoks, sc)
+    r.cache.sync_check()
+    got = O.f16_to_f32(from_dev(od))
+    row = 0
+    for sid, P0, n in zip(sids, prefixes, ntoks):
+        kk = np.stack(r.logical_k[(sid, 0)])
+        vv = np.stack(r.logical_v[(sid, 0)])
+        for j in range(n):
+            pos = P0 + j
+            qj = O.rope_row(q[row], r.cos, r.sin, pos) if r.rope else q[row]
+            ref = O.decode_one(qj, kk[:pos + 1], vv[:pos + 1], sc)
+            check_close(got[row], ref, f"prefill seq {sid} row {j} pos {pos}")
+            row += 1
+
+
+@pytest.mark.parametrize("D,G,bs,rope", [(128, 1, 16, True), (128, 4, 32, True), (64, 8, 16, False),
+                                         (128, 3, 16, True), (64, 2, 32, True)])
+def test_prefill_attention_over_cached_prefix(D, G, bs, rope):
+    """Paged causal prefill (replacing kernels::attention_prefill): prompts
+    of several lengths (one token to several CTAs of query rows), alone and
+    after a cached prefix, in one call; the grouped query heads (G = 3 is
+    padded to 4 in the CTA's rows) share their KV head."""
+    Hkv = 2
+    r = Run.create(L=1, Hq=Hkv * G, Hkv=Hkv, D=D, bs=bs, max_seq_len=400, max_batch=5, rope=rope,
+                   permute_seed=17)
+    prefixes = [0, 0, 5, 100, 33]
+    ntoks = [1, 130, 17, 64, 200]
+    sids = [r.allocate(400) for _ in prefixes]
+    _prefill_and_check(r, sids, prefixes, ntoks, seed=1234 + D + G)
+    r.check_pool_bit_exact()
+
+
 def test_single_long_sequence_many_splits():
     """One KV head, one long sequence: every worker gets a slice of the same
     unit, so the merge pass combines hundreds of partials."""

@@ -106,3 +106,34 @@ def test_append_byte_identical_to_reference_manager():
         assert np.array_equal(d2h(rv, n * H * D), d2h(ov, n * H * D)), f"V layer {l}"
         assert np.array_equal(d2h(ok, n * H * D).reshape(n, H, D), ks[l])
     rc.close()
+
+
+@pytest.mark.parametrize("Hq,Hkv,S,D", [(8, 8, 1, 64), (4, 4, 97, 128), (8, 2, 200, 64)])
+def test_prefill_matches_reference_kernel(Hq, Hkv, S, D):
+    """Our paged prefill over a fresh prompt vs the reference's own
+    kernels::attention_prefill on the same Q/K/V (its [B][H][S][D] layout,
+    K/V repeated per query head for GQA: the reference has no grouping)."""
+    import torch
+    scale = 1.0 / math.sqrt(D)
+    q = O.normal_f16((S, Hq, D), 71 + S)
+    k = O.normal_f16((S, Hkv, D), 72 + S)
+    v = O.normal_f16((S, Hkv, D), 73 + S)
+    G = Hq // Hkv
+    qh = np.ascontiguousarray(q.transpose(1, 0, 2))[None]  # [1][Hq][S][D]
+    kh = np.ascontiguousarray(np.repeat(k, G, axis=1).transpose(1, 0, 2))[None]
+    vh = np.ascontiguousarray(np.repeat(v, G, axis=1).transpose(1, 0, 2))[None]
+    qd, kd, vd = to_dev(qh), to_dev(kh), to_dev(vh)
+    od = torch.zeros((1, Hq, S, D), dtype=torch.int16, device="cuda")
+    ref_lib.attention_prefill(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(), scale, 1, Hq, S, D)
+    torch.cuda.synchronize()
+    ref = O.f16_to_f32(from_dev(od)).reshape(Hq, S, D).transpose(1, 0, 2)  # [S][Hq][D]
+    cache = T.KVCache(num_layers=1, num_kv_heads=Hkv, head_dim=D, max_seq_len=S,
+                      max_batch_size=1, num_q_heads=Hq)
+    sid = cache.allocate_sequence(S)
+    kd2, vd2, qd2 = to_dev(k), to_dev(v), to_dev(q)
+    cache.append_kv(sid, 0, kd2.data_ptr(), vd2.data_ptr(), S)
+    o2 = torch.zeros((S, Hq, D), dtype=torch.int16, device="cuda")
+    cache.prefill_attention(0, qd2.data_ptr(), o2.data_ptr(), [sid], [S], scale)
+    cache.sync_check()
+    got = O.f16_to_f32(from_dev(o2)).reshape(S, Hq, D)
+    check_close(got, ref, f"prefill ours vs reference kernel S={S} Hq={Hq} Hkv={Hkv}")

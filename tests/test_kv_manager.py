@@ -175,6 +175,29 @@ def test_attention_step_validates_then_refuses_compute():
     assert c.pool_stats().used_blocks == 1  # the block taken at allocation, nothing grown
 
 
+def test_prefill_attention_validates_arguments():
+    """tl_prefill_attention: bad layer, null pointers, unknown or duplicate
+    sequences, and query counts outside [1, written tokens] are refused."""
+    c = make(2, 4, 64, 32, 2)
+    sid = c.allocate_sequence(16)
+    with pytest.raises(T.InvalidArgument) as e:
+        c.prefill_attention(5, 16, 16, [sid], [1])
+    assert "Invalid layer_idx" in str(e.value)
+    with pytest.raises(T.InvalidArgument) as e:
+        c.prefill_attention(0, None, 16, [sid], [1])
+    assert "query is null" in str(e.value)
+    with pytest.raises(T.NotFound):
+        c.prefill_attention(0, 16, 16, [sid + 5], [1])
+    with pytest.raises(T.InvalidArgument) as e:
+        c.prefill_attention(0, 16, 16, [sid, sid], [1, 1])
+    assert "duplicate" in str(e.value)
+    with pytest.raises(T.InvalidArgument) as e:  # nothing written yet
+        c.prefill_attention(0, 16, 16, [sid], [1])
+    assert "num_tokens must be in" in str(e.value)
+    with pytest.raises(T.InvalidArgument):
+        c.prefill_attention(0, 16, 16, [sid], [1, 2])
+
+
 def test_advance_clamps_to_capacity():  # :262-273
     c = make(2, 4, 8, 32, 2)
     sid = c.allocate_sequence(5)

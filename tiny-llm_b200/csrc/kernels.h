@@ -120,6 +120,31 @@ struct DecodeArgs {
     int prefix[kMaxDecodeSeqs + 1];  // prefix sums of unit_slots(tiles) per sequence
 };
 
+// One causal prefill launch over up to kMaxPrefillSeqs sequences of one
+// layer: sequence b's ntok[b] query rows (packed in q/o from row row_off[b],
+// [rows][Hq][D] fp16) sit at positions [written[b] - ntok[b], written[b])
+// and attend the sequence's tokens up to their own position. CTA x of the
+// grid serves sequence b for cta_prefix[b] <= x < cta_prefix[b + 1], one CTA
+// per 64 (query, head) rows (group padded to group_pad); grid.y = KV head.
+constexpr int kMaxPrefillSeqs = 64;
+struct PrefillArgs {
+    PoolGeom g;
+    const void *q;
+    void *o;
+    const float *rope_cos;  // non-null: Q rotated at each row's position
+    const float *rope_sin;
+    int rope_max_pos;
+    int layer;
+    int group, group_pad;
+    float scale_log2;
+    int nseq;
+    int slot[kMaxPrefillSeqs];
+    int written[kMaxPrefillSeqs];
+    int ntok[kMaxPrefillSeqs];
+    int row_off[kMaxPrefillSeqs];
+    int cta_prefix[kMaxPrefillSeqs + 1];
+};
+
 // Sizes the kernels need from the host.
 inline int partial_row_floats(int head_dim) { return head_dim + 4; }
 int decode_workers_per_cta();
@@ -131,6 +156,8 @@ cudaError_t launch_apply_deltas(const DeltaArgs &a, cudaStream_t s);
 cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128);
 cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t s);
 cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s);
+int prefill_rows_per_cta();
+cudaError_t launch_prefill(const PrefillArgs &a, const void *tmap128, cudaStream_t s);
 
 
 }  // namespace tllm

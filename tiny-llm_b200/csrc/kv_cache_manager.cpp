@@ -94,6 +94,16 @@ Result<void> KVCacheManager::attentionStep(int layer_idx, const half *q, const h
                                     (int)seq_ids.size(), scale, stream));
 }
 
+Result<void> KVCacheManager::prefillAttention(int layer_idx, const half *q, half *out,
+                                              const std::vector<int> &seq_ids,
+                                              const std::vector<int> &num_tokens, float scale,
+                                              cudaStream_t stream) {
+    if (seq_ids.size() != num_tokens.size())
+        return Result<void>::err("prefillAttention: seq_ids and num_tokens differ in length");
+    return status(tl_prefill_attention(h_, layer_idx, q, out, seq_ids.data(), num_tokens.data(),
+                                       (int)seq_ids.size(), scale, stream));
+}
+
 Result<std::vector<int>> KVCacheManager::getBlockTable(int seq_id) const {
     int n = 0;
     if (tl_get_block_table(h_, seq_id, nullptr, 0, &n) != TL_OK)

@@ -959,6 +959,93 @@ int tl_attention_step(tl_cache *c, int layer, const void *q, const void *k_new, 
                        nullptr, c->cfg.rope_on_append != 0);
 }
 
+// Causal prefill attention over the paged cache (replaces
+// kernels::attention_prefill, reference kernels/attention.cu:131-237, as
+// called at src/transformer.cpp:238-242): sequence i's num_tokens[i] query
+// rows are its last num_tokens[i] written tokens, each attending the tokens
+// up to its own position.
+int tl_prefill_attention(tl_cache *c, int layer, const void *q, void *o, const int *seq_ids,
+                         const int *num_tokens, int num_seqs, float scale, tl_stream_t stream) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    const char *ctx = "prefillAttention";
+    if (layer < 0 || layer >= c->cfg.num_layers) return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, ctx, layer));
+    if (num_seqs < 0) return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": num_seqs must be >= 0");
+    if (num_seqs == 0) return TL_OK;
+    if (!q) return set_error(c, TL_ERR_INVALID_ARG, "query is null");
+    if (!o) return set_error(c, TL_ERR_INVALID_ARG, "output is null");
+    if (!seq_ids || !num_tokens) return set_error(c, TL_ERR_INVALID_ARG, "seq_ids is null");
+    if (((uintptr_t)q & 3u) || ((uintptr_t)o & 3u))
+        return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": q and o must be 4-byte aligned");
+    std::vector<const Sequence *> ss((size_t)num_seqs);
+    std::unordered_set<int> seen;
+    for (int i = 0; i < num_seqs; ++i) {
+        const Sequence *s = find_seq(c, seq_ids[i]);
+        if (!s)
+            return set_error(c, TL_ERR_NOT_FOUND,
+                             std::string(ctx) + ": sequence not found: " + std::to_string(seq_ids[i]));
+        if (!seen.insert(seq_ids[i]).second)
+            return set_error(c, TL_ERR_INVALID_ARG,
+                             std::string(ctx) + ": duplicate sequence id " + std::to_string(seq_ids[i]));
+        ss[(size_t)i] = s;
+    }
+    for (int i = 0; i < num_seqs; ++i)
+        if (num_tokens[i] <= 0 || num_tokens[i] > ss[(size_t)i]->written)
+            return set_error(c, TL_ERR_INVALID_ARG,
+                             std::string(ctx) + ": num_tokens must be in [1, written tokens] for seq " +
+                                 std::to_string(seq_ids[i]) + ": " + std::to_string(num_tokens[i]));
+    const int D = c->cfg.head_dim;
+    if (!decode_geometry_supported(c) || (D != 64 && D != 128))
+        return set_error(c, TL_ERR_UNSUPPORTED,
+                         std::string(ctx) + ": supported shapes are head_dim 64/128, block_size 16/32, "
+                                            "query group 1..8");
+    if (!c->on_device)
+        return set_error(c, TL_ERR_NO_DEVICE, std::string(ctx) + ": handle has no CUDA device (bookkeeping backend)");
+    DeviceGuard guard(c);
+    if (!c->pending.empty()) {
+        int st = flush_deltas(c, (cudaStream_t)stream);
+        if (st != TL_OK) return st;
+    }
+    if (!(scale > 0.0f)) scale = 1.0f / std::sqrt((float)D);
+    int gp = 1;
+    while (gp < c->group) gp <<= 1;
+    const int qpb = tllm::prefill_rows_per_cta() / gp;
+    long long row = 0;
+    for (int j0 = 0; j0 < num_seqs; j0 += tllm::kMaxPrefillSeqs) {
+        const int n = std::min(tllm::kMaxPrefillSeqs, num_seqs - j0);
+        tllm::PrefillArgs a{};
+        a.g = c->geom();
+        a.q = q;
+        a.o = o;
+        if (c->cfg.rope_on_append) {
+            a.rope_cos = c->rope_cos;
+            a.rope_sin = c->rope_sin;
+            a.rope_max_pos = c->cfg.max_seq_len;
+        }
+        a.layer = layer;
+        a.group = c->group;
+        a.group_pad = gp;
+        a.scale_log2 = scale * 1.4426950408889634f;
+        a.nseq = n;
+        a.cta_prefix[0] = 0;
+        for (int i = 0; i < n; ++i) {
+            const Sequence *s = ss[(size_t)(j0 + i)];
+            const int nt = num_tokens[j0 + i];
+            if (row + nt > INT32_MAX)
+                return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": too many query rows in one call");
+            a.slot[i] = s->slot;
+            a.written[i] = s->written;
+            a.ntok[i] = nt;
+            a.row_off[i] = (int)row;
+            row += nt;
+            a.cta_prefix[i + 1] = a.cta_prefix[i] + (nt + qpb - 1) / qpb;
+        }
+        cudaError_t e = tllm::launch_prefill(a, c->tmap, (cudaStream_t)stream);
+        if (e != cudaSuccess) return cuda_fail(c, e, "prefillAttention: launch failed");
+        ++c->launches;
+    }
+    return TL_OK;
+}
+
 int tl_peer_init(tl_cache *c, int rank, int world, size_t gather_bytes, void *ipc_handle) {
     if (!c) return TL_ERR_INVALID_ARG;
     if (world < 1 || world > tllm::kMaxPeers || rank < 0 || rank >= world || !ipc_handle)

@@ -43,7 +43,7 @@ EXPORTED_SYMBOLS = [
     "tl_get_pool", "tl_decode_attention", "tl_sync_check", "tl_rope_table",
     "tl_permute_free_blocks", "tl_debug_inject_alloc_failure", "tl_version",
     "tl_decode_attention_static", "tl_peer_init", "tl_peer_connect", "tl_peer_buffer",
-    "tl_decode_attention_peer", "tl_attention_step",
+    "tl_decode_attention_peer", "tl_attention_step", "tl_prefill_attention",
 ]
 
 
@@ -141,6 +141,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_get_pool": (i, [vp, C.POINTER(vp), C.POINTER(sz)]),
         "tl_decode_attention": (i, [vp, i, vp, vp, ip, i, f, vp]),
         "tl_attention_step": (i, [vp, i, vp, vp, vp, vp, ip, i, f, vp]),
+        "tl_prefill_attention": (i, [vp, i, vp, vp, ip, ip, i, f, vp]),
         "tl_sync_check": (i, [vp, vp]),
         "tl_rope_table": (None, [C.POINTER(C.c_float), C.POINTER(C.c_float), i, i, f]),
         "tl_permute_free_blocks": (i, [vp, C.c_ulonglong]),
@@ -300,6 +301,15 @@ class KVCache:
         self._check(self._lib.tl_attention_step(self._h, int(layer), q_ptr, k_ptr, v_ptr, o_ptr,
                                                 _ids(seq_ids), len(seq_ids), float(scale),
                                                 stream or None))
+
+    def prefill_attention(self, layer, q_ptr, o_ptr, seq_ids, num_tokens, scale=0.0, stream=0):
+        """Causal attention of each sequence's last num_tokens[i] written
+        tokens (rows packed sequence after sequence in q/o)."""
+        if len(num_tokens) != len(seq_ids):
+            raise InvalidArgument(TL_ERR_INVALID_ARG, "seq_ids and num_tokens differ in length")
+        self._check(self._lib.tl_prefill_attention(self._h, int(layer), q_ptr, o_ptr, _ids(seq_ids),
+                                                   _ids(num_tokens), len(seq_ids), float(scale),
+                                                   stream or None))
 
     # -- head-sharded peer gather (one process per GPU) ----------------------
     def peer_init(self, rank: int, world: int, gather_bytes: int) -> bytes:
