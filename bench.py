@@ -877,7 +877,7 @@ def main():
                                    l2="K/V of a layer (67 MB) kept in L2 across the query blocks; Q/O stream"),
                     "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak,
                                  "unit": "TFLOP/s", "frac": round(achieved / tpeak, 4), "traffic": None,
-                                 "kernel": "paged_prefill_kernel (mma.sync m16n8k16)",
+                                 "kernel": "paged_prefill_tc_kernel (tcgen05.mma, TMEM accumulators)",
                                  "peak_source": "measured cuBLAS bf16 dense (MEASURED_PEAKS.json bf16_tflops)"
                                  if pk else "fallback"},
                     "cpu_baseline": None,

@@ -156,8 +156,8 @@ cudaError_t launch_apply_deltas(const DeltaArgs &a, cudaStream_t s);
 cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128);
 cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t s);
 cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s);
-int prefill_rows_per_cta();
-cudaError_t launch_prefill(const PrefillArgs &a, const void *tmap128, cudaStream_t s);
+int prefill_tc_rows_per_cta();
+cudaError_t launch_prefill_tc(const PrefillArgs &a, const void *tmap128, cudaStream_t s);
 
 
 }  // namespace tllm

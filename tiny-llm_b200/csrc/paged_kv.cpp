@@ -1008,7 +1008,7 @@ int tl_prefill_attention(tl_cache *c, int layer, const void *q, void *o, const i
     if (!(scale > 0.0f)) scale = 1.0f / std::sqrt((float)D);
     int gp = 1;
     while (gp < c->group) gp <<= 1;
-    const int qpb = tllm::prefill_rows_per_cta() / gp;
+    const int qpb = tllm::prefill_tc_rows_per_cta() / gp;
     long long row = 0;
     for (int j0 = 0; j0 < num_seqs; j0 += tllm::kMaxPrefillSeqs) {
         const int n = std::min(tllm::kMaxPrefillSeqs, num_seqs - j0);
@@ -1039,7 +1039,7 @@ int tl_prefill_attention(tl_cache *c, int layer, const void *q, void *o, const i
             row += nt;
             a.cta_prefix[i + 1] = a.cta_prefix[i] + (nt + qpb - 1) / qpb;
         }
-        cudaError_t e = tllm::launch_prefill(a, c->tmap, (cudaStream_t)stream);
+        cudaError_t e = tllm::launch_prefill_tc(a, c->tmap, (cudaStream_t)stream);
         if (e != cudaSuccess) return cuda_fail(c, e, "prefillAttention: launch failed");
         ++c->launches;
     }
