@@ -9,33 +9,34 @@
 // tokens up to its own position (a prompt continuing a cached prefix sees
 // the prefix too).
 //
-// One CTA per (sequence, KV head, block of 128 (query, head) rows) — the M
-// of one UMMA; the query group (G heads sharing the KV head, padded to a
-// power of two G') is packed into the rows: row r = query r / G', head
-// r % G'. Two CTAs share an SM, so one's softmax runs while the other waits.
-// Six warps:
-//   warps 0-3  softmax: thread r owns row r (TMEM lane r). Loads its Q row
-//              (RoPE at its position) into shared memory once; per 64-key
-//              tile reads its S row from TMEM, masks by position, keeps the
-//              running max and sum, and writes its P row (fp16) to shared
-//              memory. O accumulates in TMEM across tiles; it is rescaled
-//              (TMEM load, multiply, store) only when a row's max grows by
-//              more than 2^8.
-//   warp 4     producer: block ids (one per lane, a window of 8 tiles
+// One CTA per (sequence, KV head, block of 256 (query, head) rows): two Q
+// tiles of 128 rows (the M of one UMMA) that share every K/V tile the CTA
+// loads, so a K/V byte feeds twice the math. The query group (G heads
+// sharing the KV head, padded to a power of two G') is packed into the
+// rows: row r = query r / G', head r % G'. Ten warps:
+//   warps 0-7  softmax: warps 4t..4t+3 own Q tile t, thread = one row (its
+//              TMEM lane). Each loads its Q row (RoPE at its position) into
+//              shared memory once; per 64-key tile reads its S row from
+//              TMEM, masks by position, keeps the running max and sum, and
+//              writes its P row (fp16) to shared memory. O accumulates in
+//              TMEM across tiles; it is rescaled (TMEM load, multiply,
+//              store) only when a row's max grows by more than 2^8.
+//   warp 8     producer: block ids (one per lane, a window of 8 tiles
 //              loaded one window ahead) and the TMA loads of the K/V tiles
 //              (4 boxes of 16 tokens x 64 halves per 64-column atom, 128-byte
 //              swizzle, no multicast, evict-last: every query block of the
 //              sequence reads them). Groups past the last token load from an
 //              out-of-range coordinate and come back as zeros.
-//   warp 5     MMA: one thread issues S = Q K^T into one of two TMEM S
-//              buffers (so S of the next tile runs during this tile's
-//              softmax) and O += P V, and commits to mbarriers; the warp owns
-//              the TMEM allocation.
+//   warp 9     MMA: one thread issues, per K/V tile, S = Q K^T for both Q
+//              tiles (into one of two TMEM S buffers each, so the next
+//              tile's S runs during this tile's softmax) and O += P V, and
+//              commits to mbarriers; the warp owns the TMEM allocation (all
+//              512 columns: per Q tile two 64-column S buffers and O).
 // Operands live in shared memory with the 128-byte swizzle: Q, K and P
-// K-major, V MN-major (rows = keys); fp16 in, fp32 accumulate. At D = 128 a
-// tile's P is written over its K (same size, already consumed by S), so a
-// stage holds K/P and V and the CTA fits twice per SM. Every wait is
-// bounded; TMEM is freed on every path.
+// K-major, V MN-major (rows = keys); fp16 in, fp32 accumulate. CTAs are
+// numbered KV head fastest, so the CTAs in flight spread over the heads
+// instead of all reading one head's K/V. Every wait is bounded; TMEM is
+// freed on every path.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -46,30 +47,30 @@
 namespace tllm {
 namespace {
 
-constexpr int kTcRows = 128;        // UMMA M: (query, head) rows per CTA
-constexpr int kTcKeys = 64;         // keys per tile (UMMA N of S, K of P V)
-constexpr int kTcThreads = 6 * 32;  // 4 softmax warps, producer, MMA
+constexpr int kTcRows = 128;               // UMMA M: rows of one Q tile
+constexpr int kQTiles = 2;                 // Q tiles per CTA, sharing each K/V tile
+constexpr int kCtaRows = kQTiles * kTcRows;
+constexpr int kTcKeys = 64;                // keys per tile (UMMA N of S, K of P V)
+constexpr int kSoftWarps = 4 * kQTiles;    // one warp per 32 TMEM lanes of a Q tile
+constexpr int kProdWarp = kSoftWarps, kMmaWarp = kSoftWarps + 1;
+constexpr int kTcThreads = (kSoftWarps + 2) * 32;
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 template <int D>
 struct TcCfg {
     static constexpr int kAtoms = D / 64;                     // 64-half column atoms
-    static constexpr int kQBytes = kAtoms * kTcRows * 128;    // Q: [atom][128 rows][128 B]
+    static constexpr int kQBytes = kAtoms * kTcRows * 128;    // one Q tile: [atom][128 rows][128 B]
     static constexpr int kAtomBytes = kTcKeys * 128;          // one atom of a K or V tile
     static constexpr int kKBytes = kAtoms * kAtomBytes;
     static constexpr int kStageBytes = 2 * kKBytes;           // K then V, each [atom][64 keys][128 B]
-    static constexpr int kNS = D == 64 ? 3 : 2;               // K/V stages
-    static constexpr int kMinBlocks = 2;                      // CTAs per SM
-    static constexpr int kPBytes = kTcRows * 128;             // one P tile: [128 rows][64 keys]
-    // At D = 128 a tile's P takes the place of its K in the stage (same
-    // size; S(kt) has read K when P(kt) is written, and the stage is only
-    // refilled after P V (kt)); at D = 64 P has two buffers of its own.
-    static constexpr bool kPInK = kKBytes == kPBytes;
-    static constexpr int kNP = kPInK ? 0 : 2;  // used as (kt & 1)
-    static constexpr int kBarBytes = 256;
-    static constexpr int kSmemBytes = kQBytes + kNS * kStageBytes + kNP * kPBytes + kBarBytes + 1024;
-    static_assert(2 * kNS + 8 <= 30, "barriers overlap the TMEM address slot");
-    static constexpr uint32_t kTmemCols = 256;                // S0 [0,64), S1 [64,128), O [128,128+D)
+    static constexpr int kNS = D == 64 ? 6 : 4;               // K/V stages
+    static constexpr int kPBytes = kTcRows * 128;             // one Q tile's P: [128 rows][64 keys]
+    static constexpr int kBarBytes = 512;
+    static constexpr int kSmemBytes =
+        kQTiles * kQBytes + kNS * kStageBytes + kQTiles * kPBytes + kBarBytes + 1024;
+    static_assert(kSmemBytes <= 227 * 1024, "prefill ring too large");
+    static_assert(2 * kNS + 6 * kQTiles + 2 <= 32, "barriers overlap the TMEM address slot");
+    static constexpr uint32_t kTmemCols = 512;  // Q tile t: S buffers at 256t + {0, 64}, O at 256t + 128
     // instruction descriptors: fp32 accumulate, fp16 A/B, A K-major, M = 128
     static constexpr uint32_t kIdescS = (1u << 4) | ((uint32_t)(kTcKeys >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
     static constexpr uint32_t kIdescO =
@@ -100,38 +101,39 @@ __device__ __forceinline__ void rope8(uint4 &x1, uint4 &x2, const float *ct, con
 constexpr float kRescaleLog2 = 8.0f;
 
 template <int D>
-__global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
+__global__ void __launch_bounds__(kTcThreads, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ PrefillArgs a) {
     using C = TcCfg<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sq = smem;
-    uint8_t *sstage = smem + C::kQBytes;
-    uint8_t *sp = sstage + C::kNS * C::kStageBytes;  // P[kNP]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sp + C::kNP * C::kPBytes);
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 30);
-    const uint32_t full_u = ptx::smem_u32(bars);    // [kNS] K/V tile landed
-    const uint32_t empty_u = full_u + 8 * C::kNS;   // [kNS] K/V stage consumed
-    const uint32_t sfull_u = empty_u + 8 * C::kNS;  // [2] S(kt) in TMEM, by kt & 1
-    const uint32_t pfull_u = sfull_u + 16;          // [2] P(kt) in smem, O rescaled
-    const uint32_t ofull_u = pfull_u + 16;          // [2] P V (kt) accumulated
-    const uint32_t done_u = ofull_u + 16;           // every MMA complete
-    const uint32_t qfull_u = done_u + 8;            // Q rows in smem
+    uint8_t *sq = smem;                                   // Q[kQTiles]
+    uint8_t *sstage = sq + kQTiles * C::kQBytes;          // K/V stages
+    uint8_t *sp = sstage + C::kNS * C::kStageBytes;       // P[kQTiles]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sp + kQTiles * C::kPBytes);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 32);
+    const uint32_t full_u = ptx::smem_u32(bars);          // [kNS] K/V tile landed
+    const uint32_t empty_u = full_u + 8 * C::kNS;         // [kNS] K/V stage consumed
+    const uint32_t sfull_u = empty_u + 8 * C::kNS;        // [t][2] S_t(kt) in TMEM, by kt & 1
+    const uint32_t pfull_u = sfull_u + 16 * kQTiles;      // [t][2] P_t(kt) in smem, O_t rescaled
+    const uint32_t ofull_u = pfull_u + 16 * kQTiles;      // [t][2] P V into O_t (kt) complete
+    const uint32_t done_u = ofull_u + 16 * kQTiles;       // every MMA complete
+    const uint32_t qfull_u = done_u + 8;                  // Q rows in smem
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const PoolGeom &g = a.g;
     const int H = g.num_kv_heads, G = a.group, Gp = a.group_pad, Hq = H * G, BS = g.block_size;
-    const int kvh = blockIdx.y;
+    const int lin = (int)(blockIdx.x + blockIdx.y * gridDim.x);
+    const int kvh = lin % H, xq = lin / H;  // KV head fastest
 
-    int lo = 0, hi = a.nseq - 1;  // sequence of this CTA: largest b with cta_prefix[b] <= blockIdx.x
+    int lo = 0, hi = a.nseq - 1;  // sequence of this CTA: largest b with cta_prefix[b] <= xq
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (a.cta_prefix[mid] <= (int)blockIdx.x) lo = mid;
+        if (a.cta_prefix[mid] <= xq) lo = mid;
         else hi = mid - 1;
     }
     const int b = lo;
-    const int qpb = kTcRows / Gp;
-    const int q0 = ((int)blockIdx.x - a.cta_prefix[b]) * qpb;
+    const int qpb = kCtaRows / Gp;
+    const int q0 = (xq - a.cta_prefix[b]) * qpb;
     const int n = a.ntok[b], written = a.written[b];
     const int pos0 = written - n;
     const int q_last = min(n, q0 + qpb) - 1;
@@ -142,33 +144,35 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
             ptx::mbar_init(full_u + 8 * s, 1);
             ptx::mbar_init(empty_u + 8 * s, 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < 2 * kQTiles; ++i) {
             ptx::mbar_init(sfull_u + 8 * i, 1);
             ptx::mbar_init(pfull_u + 8 * i, kTcRows);
             ptx::mbar_init(ofull_u + 8 * i, 1);
         }
         ptx::mbar_init(done_u, 1);
-        ptx::mbar_init(qfull_u, kTcRows);
+        ptx::mbar_init(qfull_u, kCtaRows);
         ptx::fence_barrier_init();
     }
-    if (warp == 5) ptx::tmem_alloc(ptx::smem_u32(tslot), C::kTmemCols);
+    if (warp == kMmaWarp) ptx::tmem_alloc(ptx::smem_u32(tslot), C::kTmemCols);
     ptx::tc_fence_before_sync();
     __syncthreads();
     ptx::tc_fence_after_sync();
     const uint32_t tbase = *tslot;
-    const uint32_t tmem_o = tbase + 2 * kTcKeys;
 
     // ---- softmax threads: this row's Q (RoPE at its position) -> smem,
     // while the producer already loads the first K/V tiles ----
-    const int r = threadIdx.x;  // row, for warps 0-3
-    const int qr = q0 + r / Gp, gr = r % Gp;
-    const bool row_valid = warp < 4 && qr <= q_last && gr < G;
+    const int qt = warp >> 2;                 // Q tile of a softmax warp
+    const int r = (warp & 3) * 32 + lane;     // row within the Q tile = TMEM lane
+    const int crow = qt * kTcRows + r;        // row within the CTA
+    const int qr = q0 + crow / Gp, gr = crow % Gp;
+    const bool row_valid = warp < kSoftWarps && qr <= q_last && gr < G;
     const int prow = pos0 + min(qr, q_last);
-    if (warp < 4) {
+    if (warp < kSoftWarps) {
         const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const __half *>(a.q) +
                                                           ((long long)(a.row_off[b] + qr) * Hq + kvh * G + gr) * D);
         const bool rope = a.rope_cos != nullptr && prow < a.rope_max_pos;
         if (a.rope_cos != nullptr && !rope && row_valid) atomicOr(g.err, kErrPosRange);
+        uint8_t *sqt = sq + qt * C::kQBytes;
 #pragma unroll
         for (int c = 0; c < D / 16; ++c) {  // chunk c and its rotate-half partner c + D/16
             uint4 x1 = make_uint4(0u, 0u, 0u, 0u), x2 = x1;
@@ -180,14 +184,14 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
                           a.rope_sin + (long long)prow * (D / 2) + 8 * c);
             }
             const int c2 = c + D / 16;
-            *reinterpret_cast<uint4 *>(sq + (c >> 3) * (kTcRows * 128) + swz(r, c)) = x1;
-            *reinterpret_cast<uint4 *>(sq + (c2 >> 3) * (kTcRows * 128) + swz(r, c2)) = x2;
+            *reinterpret_cast<uint4 *>(sqt + (c >> 3) * (kTcRows * 128) + swz(r, c)) = x1;
+            *reinterpret_cast<uint4 *>(sqt + (c2 >> 3) * (kTcRows * 128) + swz(r, c2)) = x2;
         }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(qfull_u);
     }
 
-    if (warp == 4) {
+    if (warp == kProdWarp) {
         // ---- producer (whole warp): lane i holds the block id of key group
         // i of an 8-tile window, loaded one window ahead; lane 0 issues ----
         const long long z_oob = 2ll * g.num_layers * g.num_blocks * (g.head_major ? H : BS);
@@ -246,24 +250,29 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
                 }
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ---- MMA issue (one thread) ----
         if (lane == 0) {
             const uint32_t q_u = ptx::smem_u32(sq), p_u = ptx::smem_u32(sp);
             bool ok = true;
-            auto issue_s = [&](int kt) -> bool {  // S(kt) = Q K^T into S buffer kt & 1
+            auto issue_s = [&](int kt) -> bool {  // S_t(kt) = Q_t K^T into S buffer kt & 1 of each Q tile
                 const int s = kt % C::kNS;
                 if (!ptx::mbar_wait_bounded(full_u + 8 * s, (uint32_t)((kt / C::kNS) & 1), kTcWaitNs)) return false;
                 ptx::tc_fence_after_sync();
                 const uint32_t k_u = ptx::smem_u32(sstage + s * C::kStageBytes);
-                const uint32_t d = tbase + (uint32_t)((kt & 1) * kTcKeys);
 #pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint64_t ad = ptx::umma_desc_sw128(q_u + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
-                    const uint64_t bd = ptx::umma_desc_sw128(k_u + (ks >> 2) * C::kAtomBytes + (ks & 3) * 32, 16, 1024);
-                    ptx::umma_f16(d, ad, bd, C::kIdescS, ks > 0 ? 1u : 0u);
+                for (int t = 0; t < kQTiles; ++t) {
+                    const uint32_t d = tbase + (uint32_t)(t * 256 + (kt & 1) * kTcKeys);
+#pragma unroll
+                    for (int ks = 0; ks < D / 16; ++ks) {
+                        const uint64_t ad = ptx::umma_desc_sw128(
+                            q_u + t * C::kQBytes + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
+                        const uint64_t bd =
+                            ptx::umma_desc_sw128(k_u + (ks >> 2) * C::kAtomBytes + (ks & 3) * 32, 16, 1024);
+                        ptx::umma_f16(d, ad, bd, C::kIdescS, ks > 0 ? 1u : 0u);
+                    }
+                    ptx::umma_commit(sfull_u + 16 * t + 8 * (kt & 1));
                 }
-                ptx::umma_commit(sfull_u + 8 * (kt & 1));
                 return true;
             };
             ok = ptx::mbar_wait_bounded(qfull_u, 0u, kTcWaitNs) && issue_s(0);
@@ -272,21 +281,25 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
                     ok = false;
                     break;
                 }
-                if (!ptx::mbar_wait_bounded(pfull_u + 8 * (kt & 1), (uint32_t)((kt >> 1) & 1), kTcWaitNs)) {
-                    ok = false;
-                    break;
-                }
-                ptx::tc_fence_after_sync();
                 const uint32_t v_u = ptx::smem_u32(sstage + (kt % C::kNS) * C::kStageBytes + C::kKBytes);
-                const uint32_t pb = C::kPInK ? ptx::smem_u32(sstage + (kt % C::kNS) * C::kStageBytes)
-                                             : p_u + (kt & 1) * C::kPBytes;
 #pragma unroll
-                for (int ks = 0; ks < kTcKeys / 16; ++ks) {
-                    const uint64_t ad = ptx::umma_desc_sw128(pb + ks * 32, 16, 1024);
-                    const uint64_t bd = ptx::umma_desc_sw128(v_u + ks * 2048, C::kAtomBytes, 1024);
-                    ptx::umma_f16(tmem_o, ad, bd, C::kIdescO, (kt > 0 || ks > 0) ? 1u : 0u);
+                for (int t = 0; t < kQTiles; ++t) {
+                    if (!ptx::mbar_wait_bounded(pfull_u + 16 * t + 8 * (kt & 1), (uint32_t)((kt >> 1) & 1),
+                                                kTcWaitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after_sync();
+#pragma unroll
+                    for (int ks = 0; ks < kTcKeys / 16; ++ks) {
+                        const uint64_t ad = ptx::umma_desc_sw128(p_u + t * C::kPBytes + ks * 32, 16, 1024);
+                        const uint64_t bd = ptx::umma_desc_sw128(v_u + ks * 2048, C::kAtomBytes, 1024);
+                        ptx::umma_f16(tbase + (uint32_t)(t * 256 + 2 * kTcKeys), ad, bd, C::kIdescO,
+                                      (kt > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    ptx::umma_commit(ofull_u + 16 * t + 8 * (kt & 1));
                 }
-                ptx::umma_commit(ofull_u + 8 * (kt & 1));
+                if (!ok) break;
                 ptx::umma_commit(empty_u + 8 * (kt % C::kNS));
             }
             if (!ok) atomicOr(g.err, kErrWaitTimeout);
@@ -296,7 +309,10 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
         }
     } else {
         // ---- softmax warps: one row per thread ----
-        const uint32_t trow = (uint32_t)(warp * 32) << 16;
+        const uint32_t trow = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(qt * 256);
+        const uint32_t tmem_o = trow + 2 * kTcKeys;
+        const uint32_t sfull_t = sfull_u + 16 * qt, pfull_t = pfull_u + 16 * qt, ofull_t = ofull_u + 16 * qt;
+        uint8_t *pb = sp + qt * C::kPBytes;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         // waits agree across the warp: the TMEM loads and stores after them
@@ -304,11 +320,11 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
         auto wait_all = [&](uint32_t bar, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, ptx::mbar_wait_bounded(bar, parity, kTcWaitNs));
         };
-        auto wait_pv = [&](int kt) -> bool {  // P V (kt) accumulated into O
-            return wait_all(ofull_u + 8 * (kt & 1), (uint32_t)((kt >> 1) & 1));
+        auto wait_pv = [&](int kt) -> bool {  // P V (kt) accumulated into this tile's O
+            return wait_all(ofull_t + 8 * (kt & 1), (uint32_t)((kt >> 1) & 1));
         };
         for (int kt = 0; kt < ntiles; ++kt) {
-            if (!wait_all(sfull_u + 8 * (kt & 1), (uint32_t)((kt >> 1) & 1))) {
+            if (!wait_all(sfull_t + 8 * (kt & 1), (uint32_t)((kt >> 1) & 1))) {
                 ok = false;
                 break;
             }
@@ -316,8 +332,8 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
             float sv[kTcKeys];
             {
                 uint32_t v0[32], v1[32];
-                ptx::tmem_ld32(tbase + trow + (uint32_t)((kt & 1) * kTcKeys), v0);
-                ptx::tmem_ld32(tbase + trow + (uint32_t)((kt & 1) * kTcKeys + 32), v1);
+                ptx::tmem_ld32(trow + (uint32_t)((kt & 1) * kTcKeys), v0);
+                ptx::tmem_ld32(trow + (uint32_t)((kt & 1) * kTcKeys + 32), v1);
                 ptx::tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -341,15 +357,17 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
                 }
             }
             const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-            // the max moves on tile 0 (key 0 <= every position, so mx is
+            // The max moves on tile 0 (key 0 <= every position, so mx is
             // finite there) and when it rises past the threshold; O then
-            // holds the earlier tiles at the old max and is rescaled
+            // holds the earlier tiles at the old max and is rescaled. P V
+            // (kt - 1) must be complete first: for the rescale and because
+            // this tile's P overwrites that tile's P.
+            if (kt > 0 && !wait_pv(kt - 1)) {
+                ok = false;
+                break;
+            }
             const bool grow = kt == 0 || mx > m + kRescaleLog2;
             if (kt > 0 && __any_sync(0xffffffffu, grow)) {
-                if (!wait_pv(kt - 1)) {
-                    ok = false;
-                    break;
-                }
                 ptx::tc_fence_after_sync();
                 const float mn = fmaxf(m, mx);
                 const float alpha = ptx::ex2(m - mn);
@@ -358,22 +376,16 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
 #pragma unroll
                 for (int c0 = 0; c0 < D; c0 += 32) {
                     uint32_t v[32];
-                    ptx::tmem_ld32(tmem_o + trow + c0, v);
+                    ptx::tmem_ld32(tmem_o + c0, v);
                     ptx::tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
-                    ptx::tmem_st32(tmem_o + trow + c0, v);
+                    ptx::tmem_st32(tmem_o + c0, v);
                 }
                 ptx::tmem_wait_st();
             } else if (kt == 0) {
                 m = mx;
             }
-            // a P buffer of its own was last read by P V (kt - 2)
-            if (!C::kPInK && kt >= 2 && !wait_pv(kt - 2)) {
-                ok = false;
-                break;
-            }
-            uint8_t *pb = C::kPInK ? sstage + (kt % C::kNS) * C::kStageBytes : sp + (kt & 1) * C::kPBytes;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < kTcKeys / 8; ++c) {
@@ -388,9 +400,10 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
                 *reinterpret_cast<uint4 *>(pb + swz(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
             l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-            // the tile holding the sequence's last token: V rows past it
-            // (stale data of the block) are zeroed so that 0 * V stays 0
-            if (key0 + kTcKeys > written && written > key0) {
+            // The tile holding the sequence's last token: V rows past it
+            // (stale data of the block) are zeroed so that 0 * V stays 0. Q
+            // tile 0 does it; P V of tile 1 is issued after tile 0's P.
+            if (qt == 0 && key0 + kTcKeys > written && written > key0) {
                 uint8_t *vp = sstage + (kt % C::kNS) * C::kStageBytes + C::kKBytes;
                 const int first_bad = written - key0;
                 const int nchunks = (kTcKeys - first_bad) * C::kAtoms * 8;
@@ -402,7 +415,7 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
             }
             ptx::fence_proxy_async_smem();
             ptx::tc_fence_before_sync();
-            ptx::mbar_arrive(pfull_u + 8 * (kt & 1));
+            ptx::mbar_arrive(pfull_t + 8 * (kt & 1));
         }
         if (ok && !wait_pv(ntiles - 1)) ok = false;
         if (!ok) {
@@ -415,7 +428,7 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += 32) {
                 uint32_t v[32];
-                ptx::tmem_ld32(tmem_o + trow + c0, v);
+                ptx::tmem_ld32(tmem_o + c0, v);
                 ptx::tmem_wait_ld();
                 if (row_valid) {
 #pragma unroll
@@ -436,7 +449,7 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
     // ---- teardown: every MMA has completed (or its wait gave up); free TMEM ----
     ptx::tc_fence_before_sync();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         ptx::tc_fence_after_sync();
         ptx::tmem_dealloc(tbase, C::kTmemCols);
     }
@@ -444,7 +457,6 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
 
 template <int D>
 cudaError_t launch_prefill_tc_t(const PrefillArgs &a, const void *tmap128, cudaStream_t s) {
-    static_assert(TcCfg<D>::kSmemBytes * TcCfg<D>::kMinBlocks <= 228 * 1024 - 2048, "prefill ring too large");
     cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          TcCfg<D>::kSmemBytes);
     if (e != cudaSuccess) return e;
@@ -460,7 +472,7 @@ cudaError_t launch_prefill_tc_t(const PrefillArgs &a, const void *tmap128, cudaS
 
 }  // namespace
 
-int prefill_tc_rows_per_cta() { return kTcRows; }
+int prefill_tc_rows_per_cta() { return kCtaRows; }
 
 cudaError_t launch_prefill_tc(const PrefillArgs &a, const void *tmap128, cudaStream_t s) {
     switch (a.g.head_dim) {
