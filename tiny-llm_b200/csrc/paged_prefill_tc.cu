@@ -18,9 +18,11 @@
 //              TMEM lane). Each loads its Q row (RoPE at its position) into
 //              shared memory once; per 64-key tile reads its S row from
 //              TMEM, masks by position, keeps the running max and sum, and
-//              writes its P row (fp16) to shared memory. O accumulates in
-//              TMEM across tiles; it is rescaled (TMEM load, multiply,
-//              store) only when a row's max grows by more than 2^8.
+//              writes its P row (fp16 pairs, two keys per packed fp32
+//              instruction) back over the first 32 columns of that S.
+//              O accumulates in TMEM across tiles; it is rescaled (TMEM
+//              load, multiply, store) only when a row's max grows by more
+//              than 2^8.
 //   warp 8     producer: block ids (one per lane, a window of 8 tiles
 //              loaded one window ahead) and the TMA loads of the K/V tiles
 //              (4 boxes of 16 tokens x 64 halves per 64-column atom, 128-byte
@@ -32,8 +34,9 @@
 //              tile's S runs during this tile's softmax) and O += P V, and
 //              commits to mbarriers; the warp owns the TMEM allocation (all
 //              512 columns: per Q tile two 64-column S buffers and O).
-// Operands live in shared memory with the 128-byte swizzle: Q, K and P
-// K-major, V MN-major (rows = keys); fp16 in, fp32 accumulate. CTAs are
+// Operands: Q and K in shared memory (K-major), V in shared memory
+// (MN-major, rows = keys), all with the 128-byte swizzle; P is the A
+// operand of P V straight from TMEM. fp16 in, fp32 accumulate. CTAs are
 // numbered KV head fastest, so the CTAs in flight spread over the heads
 // instead of all reading one head's K/V. Every wait is bounded; TMEM is
 // freed on every path.
@@ -63,14 +66,14 @@ struct TcCfg {
     static constexpr int kAtomBytes = kTcKeys * 128;          // one atom of a K or V tile
     static constexpr int kKBytes = kAtoms * kAtomBytes;
     static constexpr int kStageBytes = 2 * kKBytes;           // K then V, each [atom][64 keys][128 B]
-    static constexpr int kNS = D == 64 ? 6 : 4;               // K/V stages
-    static constexpr int kPBytes = kTcRows * 128;             // one Q tile's P: [128 rows][64 keys]
+    static constexpr int kNS = D == 64 ? 8 : 5;               // K/V stages
     static constexpr int kBarBytes = 512;
-    static constexpr int kSmemBytes =
-        kQTiles * kQBytes + kNS * kStageBytes + kQTiles * kPBytes + kBarBytes + 1024;
+    static constexpr int kSmemBytes = kQTiles * kQBytes + kNS * kStageBytes + kBarBytes + 1024;
     static_assert(kSmemBytes <= 227 * 1024, "prefill ring too large");
     static_assert(2 * kNS + 6 * kQTiles + 2 <= 32, "barriers overlap the TMEM address slot");
-    static constexpr uint32_t kTmemCols = 512;  // Q tile t: S buffers at 256t + {0, 64}, O at 256t + 128
+    // Q tile t: S buffers at 256t + {0, 64} (P of the tile over the first 32
+    // columns of its S), O at 256t + 128
+    static constexpr uint32_t kTmemCols = 512;
     // instruction descriptors: fp32 accumulate, fp16 A/B, A K-major, M = 128
     static constexpr uint32_t kIdescS = (1u << 4) | ((uint32_t)(kTcKeys >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
     static constexpr uint32_t kIdescO =
@@ -86,10 +89,14 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) { return row * 128 +
 // even, as the append kernel rotates K.
 __device__ __forceinline__ void rope8(uint4 &x1, uint4 &x2, const float *ct, const float *st) {
     __half *h1 = reinterpret_cast<__half *>(&x1), *h2 = reinterpret_cast<__half *>(&x2);
+    const float4 c0 = __ldg(reinterpret_cast<const float4 *>(ct)), c1 = __ldg(reinterpret_cast<const float4 *>(ct) + 1);
+    const float4 s0 = __ldg(reinterpret_cast<const float4 *>(st)), s1 = __ldg(reinterpret_cast<const float4 *>(st) + 1);
+    const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float u = __half2float(h1[i]), v = __half2float(h2[i]);
-        const float c = ct[i], s = st[i];
+        const float c = cv[i], s = sv[i];
         h1[i] = __float2half_rn(__fsub_rn(__fmul_rn(u, c), __fmul_rn(v, s)));
         h2[i] = __float2half_rn(__fadd_rn(__fmul_rn(v, c), __fmul_rn(u, s)));
     }
@@ -108,13 +115,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sq = smem;                                   // Q[kQTiles]
     uint8_t *sstage = sq + kQTiles * C::kQBytes;          // K/V stages
-    uint8_t *sp = sstage + C::kNS * C::kStageBytes;       // P[kQTiles]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sp + kQTiles * C::kPBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sstage + C::kNS * C::kStageBytes);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 32);
     const uint32_t full_u = ptx::smem_u32(bars);          // [kNS] K/V tile landed
     const uint32_t empty_u = full_u + 8 * C::kNS;         // [kNS] K/V stage consumed
     const uint32_t sfull_u = empty_u + 8 * C::kNS;        // [t][2] S_t(kt) in TMEM, by kt & 1
-    const uint32_t pfull_u = sfull_u + 16 * kQTiles;      // [t][2] P_t(kt) in smem, O_t rescaled
+    const uint32_t pfull_u = sfull_u + 16 * kQTiles;      // [t][2] P_t(kt) in TMEM, O_t rescaled
     const uint32_t ofull_u = pfull_u + 16 * kQTiles;      // [t][2] P V into O_t (kt) complete
     const uint32_t done_u = ofull_u + 16 * kQTiles;       // every MMA complete
     const uint32_t qfull_u = done_u + 8;                  // Q rows in smem
@@ -253,7 +259,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp == kMmaWarp) {
         // ---- MMA issue (one thread) ----
         if (lane == 0) {
-            const uint32_t q_u = ptx::smem_u32(sq), p_u = ptx::smem_u32(sp);
+            const uint32_t q_u = ptx::smem_u32(sq);
             bool ok = true;
             auto issue_s = [&](int kt) -> bool {  // S_t(kt) = Q_t K^T into S buffer kt & 1 of each Q tile
                 const int s = kt % C::kNS;
@@ -292,10 +298,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     ptx::tc_fence_after_sync();
 #pragma unroll
                     for (int ks = 0; ks < kTcKeys / 16; ++ks) {
-                        const uint64_t ad = ptx::umma_desc_sw128(p_u + t * C::kPBytes + ks * 32, 16, 1024);
+                        const uint32_t pa = tbase + (uint32_t)(t * 256 + (kt & 1) * kTcKeys + ks * 8);
                         const uint64_t bd = ptx::umma_desc_sw128(v_u + ks * 2048, C::kAtomBytes, 1024);
-                        ptx::umma_f16(tbase + (uint32_t)(t * 256 + 2 * kTcKeys), ad, bd, C::kIdescO,
-                                      (kt > 0 || ks > 0) ? 1u : 0u);
+                        ptx::umma_f16_ta(tbase + (uint32_t)(t * 256 + 2 * kTcKeys), pa, bd, C::kIdescO,
+                                         (kt > 0 || ks > 0) ? 1u : 0u);
                     }
                     ptx::umma_commit(ofull_u + 16 * t + 8 * (kt & 1));
                 }
@@ -312,7 +318,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t trow = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(qt * 256);
         const uint32_t tmem_o = trow + 2 * kTcKeys;
         const uint32_t sfull_t = sfull_u + 16 * qt, pfull_t = pfull_u + 16 * qt, ofull_t = ofull_u + 16 * qt;
-        uint8_t *pb = sp + qt * C::kPBytes;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         // waits agree across the warp: the TMEM loads and stores after them
@@ -342,32 +347,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             const int key0 = kt * kTcKeys;
-            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // 4 independent chains
-            if (key0 + kTcKeys - 1 <= prow) {
+            if (key0 + kTcKeys - 1 > prow) {  // keys past this row's position
 #pragma unroll
-                for (int j = 0; j < kTcKeys; ++j) {
-                    sv[j] *= a.scale_log2;
-                    mx4[j & 3] = fmaxf(mx4[j & 3], sv[j]);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kTcKeys; ++j) {
-                    sv[j] = key0 + j <= prow ? sv[j] * a.scale_log2 : -INFINITY;
-                    mx4[j & 3] = fmaxf(mx4[j & 3], sv[j]);
-                }
+                for (int j = 0; j < kTcKeys; ++j)
+                    if (key0 + j > prow) sv[j] = -INFINITY;
             }
-            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            // max of the raw scores, then scaled (the scale is positive and
+            // rounding is monotonic, so this is the max of the scaled ones)
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // 4 independent chains
+#pragma unroll
+            for (int j = 0; j < kTcKeys; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], sv[j]);
+            const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
             // The max moves on tile 0 (key 0 <= every position, so mx is
             // finite there) and when it rises past the threshold; O then
-            // holds the earlier tiles at the old max and is rescaled. P V
-            // (kt - 1) must be complete first: for the rescale and because
-            // this tile's P overwrites that tile's P.
-            if (kt > 0 && !wait_pv(kt - 1)) {
-                ok = false;
-                break;
-            }
+            // holds the earlier tiles at the old max and is rescaled once
+            // P V (kt - 1) is complete.
             const bool grow = kt == 0 || mx > m + kRescaleLog2;
             if (kt > 0 && __any_sync(0xffffffffu, grow)) {
+                if (!wait_pv(kt - 1)) {
+                    ok = false;
+                    break;
+                }
                 ptx::tc_fence_after_sync();
                 const float mn = fmaxf(m, mx);
                 const float alpha = ptx::ex2(m - mn);
@@ -386,20 +386,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             } else if (kt == 0) {
                 m = mx;
             }
-            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+            // P = 2^(s * scale - m), two keys per packed fp32 instruction,
+            // as fp16 pairs over the first 32 columns of this tile's S
+            const uint64_t sc2 = ptx::f2_pack(a.scale_log2, a.scale_log2), nm2 = ptx::f2_pack(-m, -m);
+            uint64_t sum2[2] = {0ull, 0ull};  // two independent chains of pairs
+            uint32_t pw[kTcKeys / 2];
 #pragma unroll
-            for (int c = 0; c < kTcKeys / 8; ++c) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = ptx::ex2(sv[8 * c + 2 * e] - m), p1 = ptx::ex2(sv[8 * c + 2 * e + 1] - m);
-                    sum4[e] += p0 + p1;
-                    const __half2 h = __floats2half2_rn(p0, p1);
-                    w[e] = *reinterpret_cast<const uint32_t *>(&h);
-                }
-                *reinterpret_cast<uint4 *>(pb + swz(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int j = 0; j < kTcKeys / 2; ++j) {
+                float y0, y1;
+                ptx::f2_unpack(ptx::f2_fma(ptx::f2_pack(sv[2 * j], sv[2 * j + 1]), sc2, nm2), y0, y1);
+                const float p0 = ptx::ex2(y0), p1 = ptx::ex2(y1);
+                sum2[j & 1] = ptx::f2_add(sum2[j & 1], ptx::f2_pack(p0, p1));
+                const __half2 h = __floats2half2_rn(p0, p1);
+                pw[j] = *reinterpret_cast<const uint32_t *>(&h);
             }
-            l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+            ptx::tmem_st32(trow + (uint32_t)((kt & 1) * kTcKeys), pw);
+            {
+                float s0, s1, s2, s3;
+                ptx::f2_unpack(sum2[0], s0, s1);
+                ptx::f2_unpack(sum2[1], s2, s3);
+                l += (s0 + s1) + (s2 + s3);
+            }
             // The tile holding the sequence's last token: V rows past it
             // (stale data of the block) are zeroed so that 0 * V stays 0. Q
             // tile 0 does it; P V of tile 1 is issued after tile 0's P.
@@ -412,8 +419,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     *reinterpret_cast<uint4 *>(vp + (rem >> 3) * C::kAtomBytes + swz(key, rem & 7)) =
                         make_uint4(0u, 0u, 0u, 0u);
                 }
+                ptx::fence_proxy_async_smem();
             }
-            ptx::fence_proxy_async_smem();
+            ptx::tmem_wait_st();
             ptx::tc_fence_before_sync();
             ptx::mbar_arrive(pfull_t + 8 * (kt & 1));
         }
