@@ -179,20 +179,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const bool rope = a.rope_cos != nullptr && prow < a.rope_max_pos;
         if (a.rope_cos != nullptr && !rope && row_valid) atomicOr(g.err, kErrPosRange);
         uint8_t *sqt = sq + qt * C::kQBytes;
+        // the whole row in flight at once (one memory round trip), then
+        // chunk c rotated with its partner c + D/16, the table rows read
+        // four chunk pairs at a time
+        uint4 x[D / 8];
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c) {  // chunk c and its rotate-half partner c + D/16
-            uint4 x1 = make_uint4(0u, 0u, 0u, 0u), x2 = x1;
-            if (row_valid) {
-                x1 = __ldg(src + c);
-                x2 = __ldg(src + c + D / 16);
-                if (rope)
-                    rope8(x1, x2, a.rope_cos + (long long)prow * (D / 2) + 8 * c,
-                          a.rope_sin + (long long)prow * (D / 2) + 8 * c);
+        for (int c = 0; c < D / 8; ++c) x[c] = row_valid ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+        if (rope && row_valid) {
+            const float *ct = a.rope_cos + (long long)prow * (D / 2), *st = a.rope_sin + (long long)prow * (D / 2);
+#pragma unroll
+            for (int c0 = 0; c0 < D / 16; c0 += 4) {
+#pragma unroll
+                for (int c = c0; c < c0 + 4 && c < D / 16; ++c) rope8(x[c], x[c + D / 16], ct + 8 * c, st + 8 * c);
             }
-            const int c2 = c + D / 16;
-            *reinterpret_cast<uint4 *>(sqt + (c >> 3) * (kTcRows * 128) + swz(r, c)) = x1;
-            *reinterpret_cast<uint4 *>(sqt + (c2 >> 3) * (kTcRows * 128) + swz(r, c2)) = x2;
         }
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c)
+            *reinterpret_cast<uint4 *>(sqt + (c >> 3) * (kTcRows * 128) + swz(r, c)) = x[c];
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(qfull_u);
     }
@@ -433,22 +436,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const float inv = 1.f / l;
             uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__half *>(a.o) +
                                                    ((long long)(a.row_off[b] + qr) * Hq + kvh * G + gr) * D);
+            uint32_t v[D / 32][32];  // the whole O row, one TMEM wait
 #pragma unroll
-            for (int c0 = 0; c0 < D; c0 += 32) {
-                uint32_t v[32];
-                ptx::tmem_ld32(tmem_o + c0, v);
-                ptx::tmem_wait_ld();
-                if (row_valid) {
+            for (int c0 = 0; c0 < D / 32; ++c0) ptx::tmem_ld32(tmem_o + 32 * c0, v[c0]);
+            ptx::tmem_wait_ld();
+            if (row_valid) {
+#pragma unroll
+                for (int c0 = 0; c0 < D / 32; ++c0) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         uint32_t w[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const __half2 h = __floats2half2_rn(__uint_as_float(v[8 * c + 2 * e]) * inv,
-                                                                __uint_as_float(v[8 * c + 2 * e + 1]) * inv);
+                            const __half2 h = __floats2half2_rn(__uint_as_float(v[c0][8 * c + 2 * e]) * inv,
+                                                                __uint_as_float(v[c0][8 * c + 2 * e + 1]) * inv);
                             w[e] = *reinterpret_cast<const uint32_t *>(&h);
                         }
-                        dst[c0 / 8 + c] = make_uint4(w[0], w[1], w[2], w[3]);
+                        dst[4 * c0 + c] = make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 }
             }
