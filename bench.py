@@ -71,6 +71,11 @@ CONFIGS = {
     # prompts, Llama-3-8B GQA shape; 4 layers (every layer is the same work).
     "pf": dict(workload="prefill: 8 prompts x 4096 tokens, Llama-3-8B GQA, 4 layers",
                L=4, Hq=32, Hkv=8, D=128, bs=16, lens=[4096] * 8, rope=True),
+    # The decode step's Q/K/V projections (W8A16, the reference's default
+    # group of 128) fused with the append: Llama-3-8B shapes, 32 sequences,
+    # every layer with its own weights (26 MB each, 839 MB in all).
+    "qkv": dict(workload="decode Q/K/V projection W8A16 (group 128) + append, Llama-3-8B, 32 seqs x 32 layers",
+                L=32, Hq=32, Hkv=8, D=128, bs=16, hidden=4096, group=128, lens=[512] * 32, rope=True),
     "c5": dict(workload="c5 8B GQA continuous-batching churn: Poisson(4) arrivals, prompts "
                         "log-U[32,4096], geometric(256) generations, <=256 active, pool ~80% occupied",
                L=32, Hq=32, Hkv=8, D=128, bs=16, lens="churn", rope=True, permute=True),
@@ -585,6 +590,213 @@ def run_prefill(cfg, args, world, rank, local):
                 launches=launches, clocks=clocks, B=B, n=n)
 
 
+def _qkv_weights(cfg, L, gen):
+    import torch
+    hidden, group, Hq, Hkv, D = cfg["hidden"], cfg["group"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+    ws = []
+    for _ in range(L):
+        layer = []
+        for n in (Hq * D, Hkv * D, Hkv * D):
+            w = torch.randint(-127, 128, (hidden, n), dtype=torch.int8, device="cuda", generator=gen)
+            sc = (torch.rand((hidden // group, n), device="cuda", generator=gen) * 0.018 + 0.002).half()
+            layer += [w, sc]
+        ws.append(layer)
+    return ws
+
+
+def qkv_weight_bytes(cfg):
+    hidden, group, Hq, Hkv, D = cfg["hidden"], cfg["group"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+    n = (Hq + 2 * Hkv) * D
+    return hidden * n + (hidden // group) * n * 2
+
+
+def run_qkv(cfg, args, world, rank, local):
+    """A step = the decode step's Q/K/V projections of every layer for B
+    sequences, one token each, with K/V written into the cache at each
+    sequence's length and Q rotated (tl_project_qkv_append). value = weight
+    bytes (int8 + fp16 scales) streamed per second; the activations, Q and
+    the K/V rows are small beside them."""
+    import torch
+    import tiny_llm_b200 as T
+    L, Hq, Hkv, D, bs = cfg["L"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["bs"]
+    hidden, group = cfg["hidden"], cfg["group"]
+    lens = list(cfg["lens"])
+    B, P = len(lens), max(lens)
+    cache = T.KVCache(num_layers=L, num_kv_heads=Hkv, head_dim=D, max_seq_len=P + 8, max_batch_size=B,
+                      block_size=bs, num_q_heads=Hq, rope_on_append=cfg["rope"], rope_theta=10000.0,
+                      device=local)
+    cache.permute_free_blocks(args.seed + rank)
+    sids = [cache.allocate_sequence(P + 8) for _ in range(B)]
+    for sid in sids:
+        cache.reserve(sid, P + 1)
+        cache.advance_seq_len(sid, P)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 7919 + rank)
+    ws = _qkv_weights(cfg, L, gen)
+    x = torch.randn((L, B, hidden), dtype=torch.float16, device="cuda", generator=gen)
+    q = torch.empty((L, B, Hq * D), dtype=torch.float16, device="cuda")
+
+    def step(s=None):
+        s = s or sp
+        for l in range(L):
+            w = ws[l]
+            cache.project_qkv_append(l, x[l].data_ptr(), hidden, w[0].data_ptr(), w[1].data_ptr(),
+                                     w[2].data_ptr(), w[3].data_ptr(), w[4].data_ptr(), w[5].data_ptr(),
+                                     group, sids, q[l].data_ptr(), s)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
+    launches0 = cache.pool_stats().kernel_launches
+    a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    z.record(stream)
+    z.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(z)
+    launches = cache.pool_stats().kernel_launches - launches0
+    cache.sync_check(sp)
+    # roofline pass: one step's L launches captured in a CUDA graph and
+    # replayed (the positions are fixed and the op rewrites the same rows),
+    # so the time is the kernels' own, without the host's per-call work
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    reps = 10
+    ga, gz = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ga.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    gz.record(stream)
+    gz.synchronize()
+    k_ms = ga.elapsed_time(gz) / (reps * L)
+    del graph
+    cache.sync_check(sp)
+    # e2e: each step's activations from pinned host memory, Q back to the host
+    hx = torch.empty(x.shape, dtype=torch.float16, pin_memory=True)
+    hq = torch.empty(q.shape, dtype=torch.float16, pin_memory=True)
+    hx.copy_(x.cpu())
+    torch.cuda.synchronize()
+    barrier(world)
+    ea, ez = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for _ in range(args.steps):
+        x.copy_(hx, non_blocking=True)
+        step()
+        hq.copy_(q, non_blocking=True)
+    ez.record(stream)
+    ez.synchronize()
+    e2e_ms = ea.elapsed_time(ez)
+    cache.sync_check(sp)
+    # CPU baseline: the oracle's restatement of the reference matmul (fp32,
+    # OpenMP) on one layer's three projections for every row
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        import numpy as np
+        import oracle as O
+        xs = x[0].cpu().numpy().view(np.uint16)
+        t0 = time.perf_counter()
+        for j in range(3):
+            O.w8a16_matmul(xs, ws[0][2 * j].cpu().numpy(), ws[0][2 * j + 1].cpu().numpy().view(np.uint16), group)
+        el = time.perf_counter() - t0
+        cpu = {"value": round(qkv_weight_bytes(cfg) / el / 1e9, 3), "unit": "GB/s",
+               "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"one layer's Q/K/V projections for all {B} rows (oracle fp32 restatement of "
+                         "kernels::w8a16_matmul, OpenMP), the K/V append not included"}
+    cache.close()
+    wb = qkv_weight_bytes(cfg)
+    io = B * hidden * 2 + B * Hq * D * 2 + 2 * B * Hkv * D * 2
+    return dict(ms=ms, bytes=(wb + io) * L * args.steps, wbytes=wb * L * args.steps, k_ms=k_ms,
+                graph_ms_per_step=k_ms * L,
+                k_bytes=wb + io, e2e_ms=e2e_ms, h2d=hx.numel() * 2, d2h=hq.numel() * 2,
+                launches=launches, clocks=clocks, B=B, cpu=cpu)
+
+
+def run_reference_qkv(cfg, args, world, rank, local):
+    """The reference's own decode-step projections and append, unchanged:
+    three kernels::w8a16_matmul per layer into q/k/v buffers (given all B
+    rows at once, which the reference engine never does) and
+    KVCacheManager::appendKV of each sequence's row. No RoPE (the reference
+    has none)."""
+    import torch
+    lib, why = load_ref()
+    if lib is None:
+        return None, why
+    L, Hq, Hkv, D = cfg["L"], cfg["Hq"], cfg["Hkv"], cfg["D"]
+    hidden, group = cfg["hidden"], cfg["group"]
+    B, P = len(cfg["lens"]), max(cfg["lens"])
+    h = C.c_void_p()
+    if lib.ref_kv_create(L, Hkv, D, P + 8, B, C.byref(h)) != 0:
+        return None, "reference KVCacheManager::create failed: " + lib.ref_last_error().decode()
+    sids = []
+    for _ in range(B):
+        sid = C.c_int()
+        assert lib.ref_kv_allocate(h, P + 8, C.byref(sid)) == 0
+        assert lib.ref_kv_advance(h, sid.value, P) == 0
+        sids.append(sid.value)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 7919 + rank)
+    ws = _qkv_weights(cfg, L, gen)
+    x = torch.randn((L, B, hidden), dtype=torch.float16, device="cuda", generator=gen)
+    q = torch.empty((L, B, Hq * D), dtype=torch.float16, device="cuda")
+    kb = torch.empty((B, Hkv * D), dtype=torch.float16, device="cuda")
+    vb = torch.empty_like(kb)
+    row = Hkv * D * 2
+
+    def step():
+        for l in range(L):
+            w = ws[l]
+            for out, j, n in ((q[l], 0, Hq * D), (kb, 1, Hkv * D), (vb, 2, Hkv * D)):
+                rc = lib.ref_w8a16_matmul(x[l].data_ptr(), w[2 * j].data_ptr(), w[2 * j + 1].data_ptr(),
+                                          out.data_ptr(), B, n, hidden, group, sp)
+                assert rc == 0, lib.ref_last_error().decode()
+            for b, sid in enumerate(sids):
+                rc = lib.ref_kv_append(h, sid, l, kb.data_ptr() + b * row, vb.data_ptr() + b * row, 1, sp)
+                assert rc == 0, lib.ref_last_error().decode()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    time.sleep(0.3)
+    a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    z.record(stream)
+    z.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(z)
+    hx = torch.empty(x.shape, dtype=torch.float16, pin_memory=True)
+    hq = torch.empty(q.shape, dtype=torch.float16, pin_memory=True)
+    hx.copy_(x.cpu())
+    torch.cuda.synchronize()
+    ea, ez = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for _ in range(args.steps):
+        x.copy_(hx, non_blocking=True)
+        step()
+        hq.copy_(q, non_blocking=True)
+    ez.record(stream)
+    ez.synchronize()
+    e2e_ms = ea.elapsed_time(ez)
+    lib.ref_kv_destroy(h)
+    wb = qkv_weight_bytes(cfg) * L * args.steps
+    return dict(ms=ms, wbytes=wb, e2e_ms=e2e_ms, h2d=hx.numel() * 2, d2h=hq.numel() * 2, clocks=clocks,
+                B=B), None
+
+
 # ---------------------------------------------------------- reference path --
 
 def load_ref():
@@ -599,6 +811,8 @@ def load_ref():
     lib.ref_kv_advance.argtypes = [vp, i, i]
     lib.ref_kv_destroy.argtypes = [vp]
     lib.ref_attention_decode.argtypes = [vp, vp, vp, vp, f, i, i, i, i, vp]
+    if hasattr(lib, "ref_w8a16_matmul"):
+        lib.ref_w8a16_matmul.argtypes = [vp, vp, vp, vp, i, i, i, i, vp]
     lib.ref_last_error.restype = C.c_char_p
     return lib, None
 
@@ -820,6 +1034,35 @@ def main():
         elif args.config == "pf":
             res, why = None, ("reference arm covers the decode configs; the reference prefill kernel "
                               "is compared in tests/test_gpu_reference.py")
+        elif args.config == "qkv":
+            res, why = run_reference_qkv(cfg, args, world, rank, local)
+            if res is not None:
+                ms = barrier_max(res["ms"], world)
+                wbt = barrier_sum(res["wbytes"], world)
+                e2e_ms = barrier_max(res["e2e_ms"], world)
+                if rank == 0:
+                    value = wbt / (ms / 1e3) / 1e9
+                    ev = wbt / (e2e_ms / 1e3) / 1e9
+                    line = {"impl": "reference", "metric": "decode QKV projection + append, weight GB/s",
+                            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+                            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                            "dtype": "int8 weights x f16 activations (fp32 accumulate)",
+                            "data": "synthetic seeded int8 weights, fp16 scales and activations",
+                            "config": dict(base_config, global_batch=res["B"] * world, hidden=cfg["hidden"],
+                                           group_size=cfg["group"],
+                                           layout="reference contiguous slots; three w8a16_matmul + appendKV per layer"),
+                            "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": 0,
+                                             "kind": "reference",
+                                             "sample": "the reference's own CUDA path (kernels::w8a16_matmul x3 + appendKV memcpys per layer) rebuilt for sm_100a, on the GPU: the reference has no host implementation of this path"},
+                            "e2e": {"value": round(ev, 2), "unit": "GB/s", "h2d_bytes_per_step": res["h2d"],
+                                    "d2h_bytes_per_step": res["d2h"]},
+                            "clocks": res["clocks"]}
+                    print(json.dumps(line), flush=True)
+                if world > 1:
+                    import torch.distributed as dist
+                    dist.destroy_process_group()
+                return
         else:
             res, why = run_reference(cfg, args, world, rank, local)
         if res is None:
@@ -882,6 +1125,38 @@ def main():
                                  if pk else "fallback"},
                     "cpu_baseline": None,
                     "e2e": {"value": round(fl / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                            "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
+                    "clocks": res["clocks"], "gpu_launches": res["launches"]}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    if args.config == "qkv":
+        res = run_qkv(cfg, args, world, rank, local)
+        ms = barrier_max(res["ms"], world)
+        wbt = barrier_sum(res["wbytes"], world)
+        e2e_ms = barrier_max(res["e2e_ms"], world)
+        if rank == 0:
+            achieved = res["k_bytes"] / (res["k_ms"] / 1e3) / 1e9
+            line = {"metric": "decode QKV projection + append, weight GB/s", "value": round(wbt / (ms / 1e3) / 1e9, 2),
+                    "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "int8 weights x f16 activations (fp32 accumulate)",
+                    "data": "synthetic seeded int8 weights, fp16 scales and activations (no checkpoint)",
+                    "config": dict({k: v for k, v in base_config.items() if k not in ("flow",)},
+                                   global_batch=res["B"] * world, hidden=cfg["hidden"], group_size=cfg["group"],
+                                   step="per layer: Q/K/V projections of every sequence's token, K/V into the pool, Q rotated",
+                                   l2="839 MB of weights per step, each layer's read once; no flush needed"),
+                    "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                 "frac": round(achieved / peak, 4), "traffic": None,
+                                 "kernel": "qkv_append_kernel (W8A16 mma.sync, split-K, fused append)",
+                                 "us_per_launch": round(res["k_ms"] * 1e3, 2),
+                                 "timed_as": "the step's launches replayed from a CUDA graph (kernel time without host calls)",
+                                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},
+                    "cpu_baseline": res["cpu"],
+                    "e2e": {"value": round(wbt / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                             "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
                     "clocks": res["clocks"], "gpu_launches": res["launches"]}
             print(json.dumps(line), flush=True)

@@ -92,6 +92,14 @@ class KVCacheManager {
     Result<void> prefillAttention(int layer_idx, const half *q, half *out, const std::vector<int> &seq_ids,
                                   const std::vector<int> &num_tokens, float scale = 0.0f,
                                   cudaStream_t stream = 0);
+    // The decode step's Q/K/V projections (W8A16, weights in the reference's
+    // [K][N] int8 + [K/group][N] fp16-scale layout) with K and V written
+    // straight into the cache at each sequence's current length and Q into
+    // q_out (rotated like K when the cache rotates on append).
+    Result<void> projectQKVAppend(int layer_idx, const half *x, int hidden, const int8_t *wq, const half *sq,
+                                  const int8_t *wk, const half *sk, const int8_t *wv, const half *sv,
+                                  int group_size, const std::vector<int> &seq_ids, half *q_out,
+                                  cudaStream_t stream = 0);
     Result<std::vector<int>> getBlockTable(int seq_id) const;
     tl_pool_stats getPoolStats() const noexcept;
     Result<void> syncCheck(cudaStream_t stream = 0);

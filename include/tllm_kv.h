@@ -199,6 +199,27 @@ int tl_attention_step(tl_cache *cache, int layer, const void *q, const void *k_n
 int tl_prefill_attention(tl_cache *cache, int layer, const void *q, void *o, const int *seq_ids,
                          const int *num_tokens, int num_seqs, float scale, tl_stream_t stream);
 
+/* Q/K/V projections of one decode token per sequence with K and V written
+ * straight into the cache, replacing the decode step's three
+ * kernels::w8a16_matmul calls and its appendKV (reference
+ * src/transformer.cpp:209-226; kernels/w8a16_matmul.cu:119-235;
+ * src/kv_cache.cpp:206-233). x: [num_seqs][hidden] fp16 (row i = sequence
+ * seq_ids[i]); wq/wk/wv: int8 [hidden][Hq*D] / [hidden][Hkv*D] row-major,
+ * sq/sk/sv: fp16 [hidden/group_size][same columns] (the reference's
+ * QuantizedWeight layout, include/tiny_llm/types.h:33-44). Each projection is
+ * sum_k x[k] * w[k][n] * scale[k/group_size][n] accumulated in fp32 and
+ * rounded to fp16; K and V rows are written at each sequence's current
+ * length in `layer` (the length does not advance, as tl_append_kv), and
+ * q_out ([num_seqs][Hq*D] fp16) receives Q; both Q and K are rotated at that
+ * position when the handle rotates on append (then decode with
+ * tl_decode_attention, which does not rotate Q). head_dim 64/128, hidden a
+ * multiple of 128, group_size 16/32/64/128; x, q_out and the scales 16-byte
+ * aligned, the weights 4-byte. Calls on different streams must not overlap
+ * (they share the handle's split-K scratch). Errors as tl_append_kv. */
+int tl_project_qkv_append(tl_cache *cache, int layer, const void *x, int hidden, const int8_t *wq,
+                          const void *sq, const int8_t *wk, const void *sk, const int8_t *wv, const void *sv,
+                          int group_size, const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream);
+
 /* ---- Head-sharded decode across the GPUs of one node -------------------
  * No reference counterpart (the reference is single-GPU). With KV heads
  * split over `world` ranks (one process per GPU), each rank's decode writes

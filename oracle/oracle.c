@@ -299,3 +299,22 @@ int or_decode_paged_f32(const uint16_t *pool, const or_pool_geom *g, int layer, 
     }
     return used;
 }
+
+/* kernels/w8a16_matmul.cu:71-93 (reference kernel) restated. */
+void or_w8a16_matmul(const uint16_t *x, const int8_t *w, const uint16_t *scales, int M, int N, int K,
+                     int group, float *out, int threads) {
+    if (M <= 0 || N <= 0 || K <= 0 || group <= 0) return;
+    const long long total = (long long)M * N;
+#pragma omp parallel for schedule(static) num_threads(threads > 1 ? threads : 1)
+    for (long long i = 0; i < total; ++i) {
+        const int r = (int)(i / N), n = (int)(i % N);
+        float sum = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const float a = or_f16_to_f32(x[(size_t)r * K + k]);
+            const float s = or_f16_to_f32(scales[(size_t)(k / group) * N + n]);
+            const float wk = (float)w[(size_t)k * N + n] * s;
+            sum = fmaf(a, wk, sum);
+        }
+        out[i] = sum;
+    }
+}

@@ -94,6 +94,17 @@ int or_decode_paged_f32(const uint16_t *pool, const or_pool_geom *g, int layer, 
                         const int *bt, int bt_stride, const int *lens, const uint16_t *q,
                         int num_q_heads, float scale, uint16_t *out, int threads);
 
+/* The reference's W8A16 projection (kernels/w8a16_matmul.cu:71-93, the
+ * reference kernel; the tiled kernel at :119-218 forms the same sums in the
+ * same order): out[r][n] = sum over k ascending of x[r][k] * w_k, where
+ * w_k = (float)w[k][n] * scale[k/group][n] rounded to fp32 and each term is
+ * fused into the running fp32 sum (nvcc compiles `sum += a * w` to an FMA).
+ * x [M][K] fp16, w [K][N] int8 row-major, scales [ceil(K/group)][N] fp16;
+ * out [M][N] fp32 (the reference rounds it to fp16). OpenMP over rows and
+ * columns when threads > 1. */
+void or_w8a16_matmul(const uint16_t *x, const int8_t *w, const uint16_t *scales, int M, int N, int K,
+                     int group, float *out, int threads);
+
 #ifdef __cplusplus
 }
 #endif

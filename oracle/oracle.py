@@ -8,6 +8,7 @@ the reference code it restates in oracle.h.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -55,6 +56,8 @@ def load():
         lib.or_decode_paged_f32.restype = C.c_int
         lib.or_decode_paged_f32.argtypes = [u16p, gp, C.c_int, C.c_int, ip, C.c_int, ip, u16p,
                                             C.c_int, C.c_float, u16p, C.c_int]
+        lib.or_w8a16_matmul.argtypes = [u16p, C.POINTER(C.c_int8), u16p, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, f32p, C.c_int]
         _lib = lib
     return _lib
 
@@ -165,3 +168,19 @@ def decode_paged_f32(pool, g: PoolGeom, layer, bt: np.ndarray, lens: np.ndarray,
                                       bt.shape[1], _i32(lens), _u16(q), num_q_heads, scale,
                                       _u16(out), threads)
     return out, used
+
+
+def w8a16_matmul(x: np.ndarray, w: np.ndarray, scales: np.ndarray, group: int, threads: int = 0) -> np.ndarray:
+    """The reference's W8A16 projection in fp32 (its exact operation order):
+    x [M][K] fp16 bits (uint16), w [K][N] int8, scales [K/group][N] fp16 bits.
+    Returns fp32 [M][N]; the reference's output is that rounded to fp16."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    w = np.ascontiguousarray(w, dtype=np.int8)
+    scales = np.ascontiguousarray(scales, dtype=np.uint16)
+    M, K = x.shape
+    N = w.shape[1]
+    assert w.shape[0] == K and scales.shape == ((K + group - 1) // group, N)
+    out = np.empty((M, N), dtype=np.float32)
+    load().or_w8a16_matmul(_u16(x), w.ctypes.data_as(C.POINTER(C.c_int8)), _u16(scales), M, N, K, group,
+                           _f32(out), threads or (os.cpu_count() or 1))
+    return out

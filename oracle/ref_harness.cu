@@ -1,18 +1,21 @@
 // extern "C" harness over the REFERENCE's own public API, compiled together
 // with the unmodified reference sources (src/kv_cache.cpp, src/logger.cpp,
-// kernels/attention.cu) into oracle/_ref/libtllm_ref.so by Makefile.ref.
+// kernels/attention.cu, kernels/w8a16_matmul.cu) into
+// oracle/_ref/libtllm_ref.so by Makefile.ref.
 //
 // TEST / BASELINE INFRASTRUCTURE ONLY: used to generate golden fixtures and
 // to time the reference arm of bench.py. It calls, unchanged:
 //   tiny_llm::KVCacheManager::create / allocateSequence / appendKV /
 //   advanceSeqLen / getCache      (include/tiny_llm/kv_cache.h:24-111)
 //   tiny_llm::kernels::attention_decode  (kernels/attention.cuh:15-18)
+//   tiny_llm::kernels::w8a16_matmul      (kernels/w8a16_matmul.cuh:22-26)
 #include <cuda_runtime.h>
 
 #include <memory>
 #include <string>
 
 #include "attention.cuh"
+#include "w8a16_matmul.cuh"
 #include "tiny_llm/kv_cache.h"
 
 namespace {
@@ -107,6 +110,19 @@ int ref_attention_prefill(const void *q, const void *k, const void *v, void *o, 
                                          static_cast<const half *>(v), static_cast<half *>(o), scale,
                                          batch, heads, seq_len, head_dim,
                                          static_cast<cudaStream_t>(stream));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        g_err = cudaGetErrorString(e);
+        return (int)e;
+    }
+    return 0;
+}
+
+int ref_w8a16_matmul(const void *x, const void *w, const void *scales, void *out, int M, int N, int K,
+                     int group, void *stream) {
+    tiny_llm::kernels::w8a16_matmul(static_cast<const half *>(x), static_cast<const int8_t *>(w),
+                                    static_cast<const half *>(scales), static_cast<half *>(out), M, N, K, group,
+                                    static_cast<cudaStream_t>(stream));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         g_err = cudaGetErrorString(e);

@@ -39,6 +39,7 @@ def load():
         lib.ref_kv_destroy.argtypes = [vp]
         lib.ref_attention_decode.argtypes = [vp, vp, vp, vp, f, i, i, i, i, vp]
         lib.ref_attention_prefill.argtypes = [vp, vp, vp, vp, f, i, i, i, i, vp]
+        lib.ref_w8a16_matmul.argtypes = [vp, vp, vp, vp, i, i, i, i, vp]
         lib.ref_last_error.restype = C.c_char_p
         _lib = lib
     return _lib
@@ -89,3 +90,10 @@ class RefCache:
         if self.h:
             self.lib.ref_kv_destroy(self.h)
             self.h = None
+
+
+def w8a16_matmul(x_dev, w_dev, s_dev, o_dev, M, N, K, group):
+    """The reference's kernels::w8a16_matmul on device pointers (fp16 out)."""
+    rc = load().ref_w8a16_matmul(x_dev, w_dev, s_dev, o_dev, M, N, K, group, None)
+    if rc != 0:
+        raise RuntimeError("reference w8a16_matmul failed: " + load().ref_last_error().decode())

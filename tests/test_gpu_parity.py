@@ -250,3 +250,81 @@ def test_all_layer_append_rejects_duplicates_and_overflow():
     with pytest.raises(T.Overflow):
         c.append_kv_all_layers([a], k.data_ptr(), k.data_ptr())
     c.sync_check()
+
+
+def _qkv_weights(hidden, ncols, group, seed):
+    """Seeded int8 weights [hidden][ncols] in [-127, 127] and fp16 scales
+    [hidden/group][ncols] in [0.002, 0.02] (the reference's QuantizedWeight
+    layout)."""
+    rng = np.random.default_rng(seed)
+    w = rng.integers(-127, 128, (hidden, ncols), dtype=np.int64).astype(np.int8)
+    s = np.float16(rng.uniform(0.002, 0.02, (hidden // group, ncols))).view(np.uint16)
+    return w, s
+
+
+def _close_f16_rows(got, exp, what):
+    """fp16 outputs of fp32 sums formed in another order: within two fp16
+    units of the row's largest magnitude (a flip of the last rounding, and
+    RoPE mixing two such values)."""
+    got = O.f16_to_f32(got).astype(np.float64).reshape(exp.shape[0], -1)
+    exp = O.f16_to_f32(exp).astype(np.float64).reshape(exp.shape[0], -1)
+    tol = 2.0 ** (np.floor(np.log2(np.abs(exp).max(axis=1, keepdims=True) + 1e-30)) - 9)
+    bad = np.abs(got - exp) > tol
+    assert not bad.any(), (f"{what}: {int(bad.sum())} of {bad.size} outside 2 fp16 units; "
+                           f"max err {np.abs(got - exp).max():.3e}")
+
+
+@pytest.mark.parametrize("D,G,bs,rope,layout,B,hidden,group", [
+    (128, 4, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 5, 512, 32),
+    (64, 2, 32, False, T.TL_LAYOUT_HEAD_MAJOR, 17, 256, 16),
+    (128, 1, 16, True, T.TL_LAYOUT_HEAD_MAJOR, 33, 1024, 128),
+    (64, 8, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 64, 384, 64),
+    (128, 4, 16, False, T.TL_LAYOUT_TOKEN_MAJOR, 70, 256, 32),
+])
+def test_project_qkv_append(D, G, bs, rope, layout, B, hidden, group):
+    """Fused W8A16 Q/K/V projection of one decode token per sequence
+    (replacing the decode step's three kernels::w8a16_matmul and appendKV):
+    Q and the K/V rows written at each sequence's length match the oracle's
+    restatement of the reference matmul rounded to fp16 (then rotated at
+    that position when the cache rotates on append); every earlier row of
+    the pool is untouched. B = 70 runs as two launches."""
+    import torch
+    Hkv = 2
+    Hq = Hkv * G
+    L = 3
+    r = Run.create(L=L, Hq=Hq, Hkv=Hkv, D=D, bs=bs, max_seq_len=160, max_batch=B, rope=rope,
+                   layout=layout, permute_seed=5)
+    lens = [(7 * i + 3) % 97 for i in range(B)]
+    sids = [r.allocate(160) for _ in range(B)]
+    for i, (sid, P) in enumerate(zip(sids, lens)):
+        if P:
+            r.prefill(sid, P, seed=300 + i)
+    x = O.normal_f16((B, hidden), 77 + B)
+    wq, sq = _qkv_weights(hidden, Hq * D, group, 1)
+    wk, sk = _qkv_weights(hidden, Hkv * D, group, 2)
+    wv, sv = _qkv_weights(hidden, Hkv * D, group, 3)
+    dev = [to_dev(a) if a.dtype == np.uint16 else torch.from_numpy(a.copy()).cuda() for a in
+           (x, wq, sq, wk, sk, wv, sv)]
+    qd = torch.full((B, Hq * D), 0x7e00, dtype=torch.int16, device="cuda")
+    layer = 1
+    r.cache.project_qkv_append(layer, dev[0].data_ptr(), hidden, dev[1].data_ptr(), dev[2].data_ptr(),
+                               dev[3].data_ptr(), dev[4].data_ptr(), dev[5].data_ptr(), dev[6].data_ptr(),
+                               group, sids, qd.data_ptr())
+    r.cache.sync_check()
+    eq = O.f32_to_f16(O.w8a16_matmul(x, wq, sq, group)).reshape(B, Hq, D)
+    ek = O.f32_to_f16(O.w8a16_matmul(x, wk, sk, group)).reshape(B, Hkv, D)
+    ev = O.f32_to_f16(O.w8a16_matmul(x, wv, sv, group)).reshape(B, Hkv, D)
+    if rope:
+        eq = np.stack([O.rope_row(eq[i], r.cos, r.sin, lens[i]) for i in range(B)])
+        ek = np.stack([O.rope_row(ek[i], r.cos, r.sin, lens[i]) for i in range(B)])
+    _close_f16_rows(from_dev(qd).reshape(B, Hq, D).reshape(B * Hq, D), eq.reshape(B * Hq, D), "Q")
+    base, n = r.cache.pool()
+    pool = d2h(base, n)
+    g = O.geom(L, Hkv, D, bs, r.cache.config.num_blocks, layout == T.TL_LAYOUT_HEAD_MAJOR)
+    for i, sid in enumerate(sids):
+        bt = np.array(r.cache.block_table(sid), np.int32)
+        k, v = O.gather(pool, g, bt, layer, lens[i] + 1)
+        _close_f16_rows(k[lens[i]], ek[i], f"K row of seq {sid}")
+        _close_f16_rows(v[lens[i]], ev[i], f"V row of seq {sid}")
+        assert r.cache.get_seq_len(sid) == lens[i]  # the length does not advance
+    r.check_pool_bit_exact()  # the prefix rows of every layer are untouched

@@ -5,7 +5,10 @@ reference sources) as a second checker, on the same seeded inputs:
   reference's behaviour);
 * our decode (through the C-ABI) vs kernels::attention_decode, within the
   attention tolerance |got - ref| <= 2e-3 + 1e-3|ref|;
-* our append vs KVCacheManager::appendKV: getCache() read-backs byte-identical.
+* our append vs KVCacheManager::appendKV: getCache() read-backs byte-identical;
+* kernels::w8a16_matmul vs the oracle's restatement rounded to fp16,
+  bit for bit (pins that oracle), and our fused Q/K/V projection + append vs
+  kernels::w8a16_matmul within two fp16 units.
 """
 import math
 import sys
@@ -137,3 +140,73 @@ def test_prefill_matches_reference_kernel(Hq, Hkv, S, D):
     cache.sync_check()
     got = O.f16_to_f32(from_dev(o2)).reshape(S, Hq, D)
     check_close(got, ref, f"prefill ours vs reference kernel S={S} Hq={Hq} Hkv={Hkv}")
+
+
+def _w8a16_case(M, N, K, group, seed):
+    rng = np.random.default_rng(seed)
+    x = O.normal_f16((M, K), seed)
+    w = rng.integers(-127, 128, (K, N), dtype=np.int64).astype(np.int8)
+    s = np.float16(rng.uniform(0.002, 0.02, ((K + group - 1) // group, N))).view(np.uint16)
+    return x, w, s
+
+
+def _reference_w8a16(x, w, s, group):
+    import torch
+    M, K = x.shape
+    N = w.shape[1]
+    xd, sd = to_dev(x), to_dev(s)
+    wd = torch.from_numpy(w.copy()).cuda()
+    od = torch.zeros((M, N), dtype=torch.int16, device="cuda")
+    ref_lib.w8a16_matmul(xd.data_ptr(), wd.data_ptr(), sd.data_ptr(), od.data_ptr(), M, N, K, group)
+    torch.cuda.synchronize()
+    return from_dev(od)
+
+
+@pytest.mark.parametrize("M,N,K,group", [(1, 256, 512, 32), (5, 128, 256, 16), (33, 384, 1024, 128),
+                                         (64, 256, 384, 64), (3, 40, 100, 8)])
+def test_oracle_w8a16_matches_reference_kernel(M, N, K, group):
+    """kernels::w8a16_matmul (its reference kernel when M*N < 4096, the tiled
+    one otherwise) equals the oracle's fp32 restatement rounded to fp16, bit
+    for bit."""
+    x, w, s = _w8a16_case(M, N, K, group, 11 + M)
+    got = _reference_w8a16(x, w, s, group)
+    exp = O.f32_to_f16(O.w8a16_matmul(x, w, s, group))
+    assert np.array_equal(got, exp), f"{int((got != exp).sum())} of {got.size} differ"
+
+
+@pytest.mark.parametrize("B,hidden,group", [(1, 512, 32), (32, 1024, 128)])
+def test_projection_matches_reference_kernel(B, hidden, group):
+    """Our fused projection (no RoPE) writes the same K/V rows, within two
+    fp16 units, as kernels::w8a16_matmul produces for k_buf_/v_buf_."""
+    import torch
+    Hkv, G, D, bs, L = 2, 4, 128, 16, 2
+    cache = T.KVCache(num_layers=L, num_kv_heads=Hkv, head_dim=D, max_seq_len=64, max_batch_size=B,
+                      block_size=bs, num_q_heads=Hkv * G)
+    sids = [cache.allocate_sequence(64) for _ in range(B)]
+    x, wq, sq = _w8a16_case(B, Hkv * G * D, hidden, group, 21)
+    _, wk, sk = _w8a16_case(B, Hkv * D, hidden, group, 22)
+    _, wv, sv = _w8a16_case(B, Hkv * D, hidden, group, 23)
+    dev = [to_dev(a) if a.dtype == np.uint16 else torch.from_numpy(a.copy()).cuda() for a in
+           (x, wq, sq, wk, sk, wv, sv)]
+    qd = torch.zeros((B, Hkv * G * D), dtype=torch.int16, device="cuda")
+    cache.project_qkv_append(0, dev[0].data_ptr(), hidden, dev[1].data_ptr(), dev[2].data_ptr(),
+                             dev[3].data_ptr(), dev[4].data_ptr(), dev[5].data_ptr(), dev[6].data_ptr(), group,
+                             sids, qd.data_ptr())
+    cache.sync_check()
+    ref = {name: O.f16_to_f32(_reference_w8a16(x, w, s, group)).astype(np.float64)
+           for name, w, s in (("q", wq, sq), ("k", wk, sk), ("v", wv, sv))}
+    got_q = O.f16_to_f32(from_dev(qd)).astype(np.float64)
+    base, n = cache.pool()
+    pool = d2h(base, n)
+    g = O.geom(L, Hkv, D, bs, cache.config.num_blocks)
+
+    rows_k, rows_v = [], []
+    for sid in sids:
+        bt = np.array(cache.block_table(sid), np.int32)
+        k, v = O.gather(pool, g, bt, 0, 1)
+        rows_k.append(O.f16_to_f32(k[0]).reshape(-1))
+        rows_v.append(O.f16_to_f32(v[0]).reshape(-1))
+    for name, got in (("q", got_q), ("k", np.stack(rows_k)), ("v", np.stack(rows_v))):
+        exp = ref[name]
+        tol = 2.0 ** (np.floor(np.log2(np.abs(exp).max(axis=1, keepdims=True) + 1e-30)) - 9)
+        assert not (np.abs(got - exp) > tol).any(), f"{name}: max err {np.abs(got - exp).max():.3e}"

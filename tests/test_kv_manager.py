@@ -198,6 +198,55 @@ def test_prefill_attention_validates_arguments():
         c.prefill_attention(0, 16, 16, [sid], [1, 2])
 
 
+def test_project_qkv_append_validates_arguments():
+    """tl_project_qkv_append: bad layer, null pointers, shapes outside the
+    kernel's (hidden not a multiple of 128, group sizes other than
+    16/32/64/128), misalignment, unknown/duplicate sequences and a full
+    sequence are refused before any device work; the bookkeeping backend
+    then reports that it has no device."""
+    c = make(2, 4, 64, 32, 2)
+    sid = c.allocate_sequence(2)
+    ok = dict(x=16, hidden=256, wq=16, sq=16, wk=16, sk=16, wv=16, sv=16, group=32, sids=[sid], q=16)
+
+    def call(layer=0, **kw):
+        a = dict(ok, **kw)
+        c.project_qkv_append(layer, a["x"], a["hidden"], a["wq"], a["sq"], a["wk"], a["sk"], a["wv"], a["sv"],
+                             a["group"], a["sids"], a["q"])
+
+    with pytest.raises(T.InvalidArgument) as e:
+        call(layer=2)
+    assert "Invalid layer_idx" in str(e.value)
+    with pytest.raises(T.InvalidArgument) as e:
+        call(x=None)
+    assert "input is null" in str(e.value)
+    with pytest.raises(T.InvalidArgument) as e:
+        call(q=None)
+    assert "q output is null" in str(e.value)
+    with pytest.raises(T.InvalidArgument):
+        call(wk=None)
+    with pytest.raises(T.InvalidArgument):
+        call(hidden=0)
+    with pytest.raises(T.Unsupported):
+        call(hidden=200)
+    with pytest.raises(T.Unsupported):
+        call(group=8)
+    with pytest.raises(T.InvalidArgument) as e:
+        call(sq=18)
+    assert "aligned" in str(e.value)
+    with pytest.raises(T.NotFound):
+        call(sids=[sid + 7])
+    with pytest.raises(T.InvalidArgument) as e:
+        call(sids=[sid, sid])
+    assert "duplicate" in str(e.value)
+    with pytest.raises(T.NoDevice):
+        call()
+    c.advance_seq_len(sid, 2)
+    with pytest.raises(T.Overflow) as e:
+        call()
+    assert "overflow" in str(e.value)
+    call(sids=[])  # nothing to do
+
+
 def test_advance_clamps_to_capacity():  # :262-273
     c = make(2, 4, 8, 32, 2)
     sid = c.allocate_sequence(5)

@@ -190,3 +190,26 @@ def test_fp32_baseline_agrees_with_fp64_oracle():
         ref = O.decode_one(q[b], ks[b], vs[b], 0.125)
         got = O.f16_to_f32(out[b])
         assert np.all(np.abs(got - ref) <= 2e-3 + 1e-3 * np.abs(ref))
+
+
+@pytest.mark.parametrize("M,N,K,group", [(1, 8, 16, 16), (5, 48, 256, 32), (3, 40, 100, 8)])
+def test_w8a16_matmul_against_float64(M, N, K, group):
+    """The W8A16 restatement (reference kernels/w8a16_matmul.cu:71-93) is the
+    product of x and the dequantised weights w * scale[k/group]: against an
+    independent float64 evaluation within fp32 summation error, and exactly
+    on a hand-sized case."""
+    rng = np.random.default_rng(M * 100 + K)
+    x = O.normal_f16((M, K), 5 + M)
+    w = rng.integers(-127, 128, (K, N), dtype=np.int64).astype(np.int8)
+    s = np.float16(rng.uniform(0.002, 0.02, ((K + group - 1) // group, N))).view(np.uint16)
+    got = O.w8a16_matmul(x, w, s, group, threads=1).astype(np.float64)
+    xf = O.f16_to_f32(x).astype(np.float64)
+    wf = w.astype(np.float64) * np.repeat(O.f16_to_f32(s).astype(np.float64), group, axis=0)[:K]
+    exp = xf @ wf
+    bound = 1e-6 * (np.abs(xf) @ np.abs(wf)) + 1e-30
+    assert (np.abs(got - exp) <= bound).all()
+    # 1 x [1, 2, -3] . w (group 2: scales 0.5 then 2)
+    x1 = O.f32_to_f16(np.array([[1.0, 2.0, -3.0]], np.float32))
+    w1 = np.array([[4], [-5], [6]], np.int8)
+    s1 = O.f32_to_f16(np.array([[0.5], [2.0]], np.float32))
+    assert O.w8a16_matmul(x1, w1, s1, 2)[0, 0] == 1 * 4 * 0.5 + 2 * -5 * 0.5 + -3 * 6 * 2.0

@@ -156,8 +156,33 @@ cudaError_t launch_apply_deltas(const DeltaArgs &a, cudaStream_t s);
 cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128);
 cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t s);
 cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s);
+// One fused Q/K/V projection + append launch (decode: one token per row).
+constexpr int kMaxQkvRows = 64;
+struct QkvArgs {
+    PoolGeom g;
+    const void *x;           // fp16 [rows][K] activations
+    const int8_t *w[3];      // Q, K, V weights: int8 [K][n[i]] row-major
+    const void *sc[3];       // fp16 scales [K / group][n[i]]
+    int n[3];                // Hq*D, Hkv*D, Hkv*D
+    int K, group, rows;
+    int num_q_heads;
+    int ksplit, kchunk;      // K split over ksplit CTAs of kchunk (a multiple of qkv_k_block())
+    void *q_out;             // fp16 [rows][Hq*D]
+    const float *rope_cos;   // RoPE on Q and K at each row's position, or nullptr
+    const float *rope_sin;
+    int rope_max_pos;
+    int layer;
+    float *partial;          // fp32 [Hq + 2 Hkv][qkv_rows_padded(rows)][D], zero between launches
+    int *counters;           // [Hq + 2 Hkv], zero between launches
+    int row_block[kMaxQkvRows];
+    int row_pos[kMaxQkvRows];
+};
+
 int prefill_tc_rows_per_cta();
 cudaError_t launch_prefill_tc(const PrefillArgs &a, const void *tmap128, cudaStream_t s);
+int qkv_k_block();
+int qkv_rows_padded(int rows);  // the kernel's row tile for a launch of `rows` rows
+cudaError_t launch_qkv_append(const QkvArgs &a, cudaStream_t s);
 
 
 }  // namespace tllm

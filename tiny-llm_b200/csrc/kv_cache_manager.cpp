@@ -104,6 +104,15 @@ Result<void> KVCacheManager::prefillAttention(int layer_idx, const half *q, half
                                        (int)seq_ids.size(), scale, stream));
 }
 
+Result<void> KVCacheManager::projectQKVAppend(int layer_idx, const half *x, int hidden, const int8_t *wq,
+                                              const half *sq, const int8_t *wk, const half *sk,
+                                              const int8_t *wv, const half *sv, int group_size,
+                                              const std::vector<int> &seq_ids, half *q_out,
+                                              cudaStream_t stream) {
+    return status(tl_project_qkv_append(h_, layer_idx, x, hidden, wq, sq, wk, sk, wv, sv, group_size,
+                                        seq_ids.data(), (int)seq_ids.size(), q_out, stream));
+}
+
 Result<std::vector<int>> KVCacheManager::getBlockTable(int seq_id) const {
     int n = 0;
     if (tl_get_block_table(h_, seq_id, nullptr, 0, &n) != TL_OK)

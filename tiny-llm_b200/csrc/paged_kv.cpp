@@ -564,6 +564,8 @@ void tl_destroy(tl_cache *c) {
         storage_free(c, c->rope_sin);
         storage_free(c, c->partial);
         storage_free(c, c->merge_counters);
+        storage_free(c, c->qkv_partial);
+        storage_free(c, c->qkv_counters);
         for (int r = 0; r < tllm::kMaxPeers; ++r)
             if (c->peer_opened[r]) cudaIpcCloseMemHandle(c->peer_bases[r]);
         storage_free(c, c->peer_region);
@@ -1043,6 +1045,150 @@ int tl_prefill_attention(tl_cache *c, int layer, const void *q, void *o, const i
         if (e != cudaSuccess) return cuda_fail(c, e, "prefillAttention: launch failed");
         ++c->launches;
     }
+    return TL_OK;
+}
+
+// Q/K/V projections (W8A16) of one decode token per sequence, with K and V
+// appended at each sequence's current length (RoPE on Q and K when the
+// handle rotates on append). Replaces the three kernels::w8a16_matmul calls
+// and the appendKV of TransformerLayer::attention's decode step (reference
+// src/transformer.cpp:209-226, kernels/w8a16_matmul.cu:119-235,
+// src/kv_cache.cpp:206-233), batched over sequences.
+int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, const int8_t *wq, const void *sq,
+                          const int8_t *wk, const void *sk, const int8_t *wv, const void *sv, int group_size,
+                          const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream) {
+    static const char *ctx = "projectQKVAppend";
+    if (!c) return TL_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= c->cfg.num_layers)
+        return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, ctx, layer));
+    if (num_seqs < 0) return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": num_seqs must be >= 0");
+    if (num_seqs == 0) return TL_OK;
+    if (!seq_ids) return set_error(c, TL_ERR_INVALID_ARG, "seq_ids is null");
+    if (!x || !q_out) return set_error(c, TL_ERR_INVALID_ARG, !x ? "input is null" : "q output is null");
+    if (!wq || !wk || !wv || !sq || !sk || !sv)
+        return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": a weight or scale pointer is null");
+    if (hidden <= 0 || group_size <= 0)
+        return set_error(c, TL_ERR_INVALID_ARG, std::string(ctx) + ": hidden and group_size must be positive");
+    const int D = c->cfg.head_dim;
+    if ((D != 64 && D != 128) || hidden % tllm::qkv_k_block() != 0 ||
+        (group_size != 16 && group_size != 32 && group_size != 64 && group_size != 128))
+        return set_error(c, TL_ERR_UNSUPPORTED,
+                         std::string(ctx) + ": supported shapes are head_dim 64/128, hidden a multiple of 128, "
+                                            "group_size 16/32/64/128");
+    auto mis = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; };
+    if (mis(x, 16) || mis(q_out, 16) || mis(sq, 16) || mis(sk, 16) || mis(sv, 16) || mis(wq, 4) || mis(wk, 4) ||
+        mis(wv, 4))
+        return set_error(c, TL_ERR_INVALID_ARG,
+                         std::string(ctx) + ": input, q output and scales must be 16-byte aligned, weights 4-byte");
+    std::vector<Sequence *> ss((size_t)num_seqs);
+    std::unordered_set<int> seen;
+    for (int i = 0; i < num_seqs; ++i) {
+        Sequence *s = find_seq(c, seq_ids[i]);
+        if (!s)
+            return set_error(c, TL_ERR_NOT_FOUND,
+                             std::string(ctx) + ": sequence not found: " + std::to_string(seq_ids[i]));
+        if (!seen.insert(seq_ids[i]).second)
+            return set_error(c, TL_ERR_INVALID_ARG,
+                             std::string(ctx) + ": duplicate sequence id " + std::to_string(seq_ids[i]));
+        if (s->len + 1 > s->max_len)
+            return set_error(c, TL_ERR_OVERFLOW,
+                             std::string(ctx) + ": cache overflow. seq " + std::to_string(seq_ids[i]) +
+                                 " Current: " + std::to_string(s->len) +
+                                 ", appending: 1, max: " + std::to_string(s->max_len));
+        ss[(size_t)i] = s;
+    }
+    if (!c->on_device)
+        return set_error(c, TL_ERR_NO_DEVICE, std::string(ctx) + ": handle has no CUDA device (bookkeeping backend)");
+    DeviceGuard guard(c);
+    const int Hkv = c->cfg.num_kv_heads, Hq = Hkv * c->group;
+    const int tiles = Hq + 2 * Hkv;
+    // split-K: about three CTAs per SM (2 and 4 measured slower); a chunk's
+    // activations stay under ~100 KB of shared memory
+    const int kblk = tllm::qkv_k_block(), nkb = hidden / kblk;
+    const int rows_max = std::min(num_seqs, tllm::kMaxQkvRows);
+    const int rpad = tllm::qkv_rows_padded(rows_max);  // the largest launch's row tile
+    const int kb_cap = std::max(1, (100 * 1024 / (2 * rpad) - 8) / kblk);
+    int ks = std::max(1, (3 * std::max(c->num_sms, 1) + tiles / 2) / tiles);
+    ks = std::min(ks, nkb);
+    int kbc = std::min((nkb + ks - 1) / ks, kb_cap);
+    ks = (nkb + kbc - 1) / kbc;
+    const size_t need = ks > 1 ? (size_t)tiles * rpad * D : 0;  // one fp32 accumulator per column tile
+    std::string why;
+    if (need > c->qkv_partial_floats) {
+        storage_free(c, c->qkv_partial);
+        c->qkv_partial = nullptr;
+        c->qkv_partial_floats = 0;
+        void *p = nullptr;
+        if (storage_alloc(c, &p, need * 4, &why))
+            return set_error(c, TL_ERR_CUDA, std::string(ctx) + ": split-K scratch allocation failed: " + why);
+        c->qkv_partial = static_cast<float *>(p);
+        c->qkv_partial_floats = need;
+    }
+    if (tiles > c->qkv_counter_n) {
+        storage_free(c, c->qkv_counters);
+        c->qkv_counters = nullptr;
+        c->qkv_counter_n = 0;
+        void *p = nullptr;
+        if (storage_alloc(c, &p, (size_t)tiles * sizeof(int), &why))
+            return set_error(c, TL_ERR_CUDA, std::string(ctx) + ": counter allocation failed: " + why);
+        c->qkv_counters = static_cast<int *>(p);
+        c->qkv_counter_n = tiles;
+    }
+    std::vector<std::pair<Sequence *, int>> undo;
+    size_t mark = c->pending.size();
+    std::vector<int> rb((size_t)num_seqs), rp((size_t)num_seqs);
+    for (int i = 0; i < num_seqs; ++i) {
+        Sequence &s = *ss[(size_t)i];
+        int st = ensure_blocks(c, s, (long long)s.len + 1, mark, &undo);
+        if (st != TL_OK) {
+            rollback(c, mark, undo);
+            return st;
+        }
+        rp[(size_t)i] = s.len;
+        rb[(size_t)i] = s.blocks[(size_t)(s.len / c->bs)];
+    }
+    if (!c->pending.empty()) {  // new blocks' table entries (the decode reads them)
+        int st = flush_deltas(c, (cudaStream_t)stream);
+        if (st != TL_OK) return st;
+    }
+    const long long nq = (long long)Hq * D;
+    for (int r0 = 0; r0 < num_seqs; r0 += tllm::kMaxQkvRows) {
+        const int n = std::min(tllm::kMaxQkvRows, num_seqs - r0);
+        tllm::QkvArgs a{};
+        a.g = c->geom();
+        a.x = static_cast<const uint16_t *>(x) + (long long)r0 * hidden;
+        a.w[0] = wq;
+        a.w[1] = wk;
+        a.w[2] = wv;
+        a.sc[0] = sq;
+        a.sc[1] = sk;
+        a.sc[2] = sv;
+        a.n[0] = Hq * D;
+        a.n[1] = a.n[2] = Hkv * D;
+        a.K = hidden;
+        a.group = group_size;
+        a.rows = n;
+        a.num_q_heads = Hq;
+        a.ksplit = ks;
+        a.kchunk = kbc * kblk;
+        a.q_out = static_cast<uint16_t *>(q_out) + r0 * nq;
+        if (c->cfg.rope_on_append) {
+            a.rope_cos = c->rope_cos;
+            a.rope_sin = c->rope_sin;
+            a.rope_max_pos = c->cfg.max_seq_len;
+        }
+        a.layer = layer;
+        a.partial = c->qkv_partial;
+        a.counters = c->qkv_counters;
+        for (int j = 0; j < n; ++j) {
+            a.row_block[j] = rb[(size_t)(r0 + j)];
+            a.row_pos[j] = rp[(size_t)(r0 + j)];
+        }
+        cudaError_t e = tllm::launch_qkv_append(a, (cudaStream_t)stream);
+        if (e != cudaSuccess) return cuda_fail(c, e, "projectQKVAppend: launch failed");
+        ++c->launches;
+    }
+    for (Sequence *s : ss) s->written = std::max(s->written, s->len + 1);
     return TL_OK;
 }
 

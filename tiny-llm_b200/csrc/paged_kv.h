@@ -86,6 +86,11 @@ struct tl_cache {
     bool peer_opened[tllm::kMaxPeers] = {};
     bool peers_connected = false;
     size_t partial_floats = 0;
+    // fused Q/K/V projection + append: split-K partials and per-tile counters
+    float *qkv_partial = nullptr;
+    size_t qkv_partial_floats = 0;
+    int *qkv_counters = nullptr;
+    int qkv_counter_n = 0;
     int max_workers = 0;
     alignas(64) unsigned char tmap[128];
 

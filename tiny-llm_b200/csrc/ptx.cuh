@@ -136,6 +136,14 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     return d;
 }
 
+// 16-byte global -> shared copy that does not hold the issuing thread;
+// src_bytes < 16 zero-fills the rest (0: nothing is read). Complete for this
+// thread after cp_async_wait_all().
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // bar.sync on a named barrier (id 1..15) among `threads` threads (a
 // multiple of 32) of the CTA.
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {

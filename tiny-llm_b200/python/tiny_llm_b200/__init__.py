@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = [
     "tl_permute_free_blocks", "tl_debug_inject_alloc_failure", "tl_version",
     "tl_decode_attention_static", "tl_peer_init", "tl_peer_connect", "tl_peer_buffer",
     "tl_decode_attention_peer", "tl_attention_step", "tl_prefill_attention",
+    "tl_project_qkv_append",
 ]
 
 
@@ -142,6 +143,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_decode_attention": (i, [vp, i, vp, vp, ip, i, f, vp]),
         "tl_attention_step": (i, [vp, i, vp, vp, vp, vp, ip, i, f, vp]),
         "tl_prefill_attention": (i, [vp, i, vp, vp, ip, ip, i, f, vp]),
+        "tl_project_qkv_append": (i, [vp, i, vp, i, vp, vp, vp, vp, vp, vp, i, ip, i, vp, vp]),
         "tl_sync_check": (i, [vp, vp]),
         "tl_rope_table": (None, [C.POINTER(C.c_float), C.POINTER(C.c_float), i, i, f]),
         "tl_permute_free_blocks": (i, [vp, C.c_ulonglong]),
@@ -310,6 +312,15 @@ class KVCache:
         self._check(self._lib.tl_prefill_attention(self._h, int(layer), q_ptr, o_ptr, _ids(seq_ids),
                                                    _ids(num_tokens), len(seq_ids), float(scale),
                                                    stream or None))
+
+    def project_qkv_append(self, layer, x_ptr, hidden, wq, sq, wk, sk, wv, sv, group_size, seq_ids, q_ptr,
+                           stream=0):
+        """W8A16 Q/K/V projections of one decode token per sequence (x rows
+        in seq_ids order); K and V are written at each sequence's current
+        length, Q into q_ptr ([num_seqs][Hq*D])."""
+        self._check(self._lib.tl_project_qkv_append(self._h, int(layer), x_ptr, int(hidden), wq, sq, wk, sk, wv,
+                                                    sv, int(group_size), _ids(seq_ids), len(seq_ids), q_ptr,
+                                                    stream or None))
 
     # -- head-sharded peer gather (one process per GPU) ----------------------
     def peer_init(self, rank: int, world: int, gather_bytes: int) -> bytes:
