@@ -82,6 +82,15 @@ CONFIGS = {
 }
 
 
+def launch_traffic(config):
+    """dram bytes read + written by one launch of the config's dominant
+    kernel, from the ncu capture recorded in profiles/dram_traffic.json."""
+    tp = ROOT / "profiles" / "dram_traffic.json"
+    if not tp.exists():
+        return None
+    return json.loads(tp.read_text()).get(config, {}).get("launch")
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -1119,7 +1128,8 @@ def main():
                                    step="append every layer's prompt K/V, causal prefill per layer, release",
                                    l2="K/V of a layer (67 MB) kept in L2 across the query blocks; Q/O stream"),
                     "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tpeak,
-                                 "unit": "TFLOP/s", "frac": round(achieved / tpeak, 4), "traffic": None,
+                                 "unit": "TFLOP/s", "frac": round(achieved / tpeak, 4),
+                                 "traffic": launch_traffic("pf"),
                                  "kernel": "paged_prefill_tc_kernel (tcgen05.mma, TMEM accumulators)",
                                  "peak_source": "measured cuBLAS bf16 dense (MEASURED_PEAKS.json bf16_tflops)"
                                  if pk else "fallback"},
@@ -1150,7 +1160,8 @@ def main():
                                    step="per layer: Q/K/V projections of every sequence's token, K/V into the pool, Q rotated",
                                    l2="839 MB of weights per step, each layer's read once; no flush needed"),
                     "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                                 "frac": round(achieved / peak, 4), "traffic": None,
+                                 "frac": round(achieved / peak, 4), "traffic": launch_traffic("qkv"),
+                                 "algorithmic_bytes_per_launch": res["k_bytes"],
                                  "kernel": "qkv_append_kernel (W8A16 mma.sync, split-K, fused append)",
                                  "us_per_launch": round(res["k_ms"] * 1e3, 2),
                                  "timed_as": "the step's launches replayed from a CUDA graph (kernel time without host calls)",
@@ -1204,7 +1215,7 @@ def main():
         value = kv / (ms / 1e3) / 1e9
         achieved = res["dec_bytes"] / (res["dec_ms"] / 1e3) / 1e9
         traffic = None
-        tp = ROOT / "profiles" / "decode_traffic.json"
+        tp = ROOT / "profiles" / "dram_traffic.json"
         if tp.exists():
             t = json.loads(tp.read_text()).get(args.config, {}).get(args.layout)
             traffic = t
