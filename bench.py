@@ -76,6 +76,10 @@ CONFIGS = {
     # every layer with its own weights (26 MB each, 839 MB in all).
     "qkv": dict(workload="decode Q/K/V projection W8A16 (group 128) + append, Llama-3-8B, 32 seqs x 32 layers",
                 L=32, Hq=32, Hkv=8, D=128, bs=16, hidden=4096, group=128, lens=[512] * 32, rope=True),
+    # Next-token sampling on the device: a decode step's logits for 32
+    # sequences over the Llama-3 vocabulary, top-p 0.9 at temperature 0.8.
+    "smp": dict(workload="next-token sampling: 32 rows x 128256 fp16 logits, top-p 0.9, T 0.8",
+                L=1, Hq=32, Hkv=8, D=128, bs=16, lens=[1] * 32, rope=False, vocab=128256),
     "c5": dict(workload="c5 8B GQA continuous-batching churn: Poisson(4) arrivals, prompts "
                         "log-U[32,4096], geometric(256) generations, <=256 active, pool ~80% occupied",
                L=32, Hq=32, Hkv=8, D=128, bs=16, lens="churn", rope=True, permute=True),
@@ -730,6 +734,67 @@ def run_qkv(cfg, args, world, rank, local):
                 launches=launches, clocks=clocks, B=B, cpu=cpu)
 
 
+def run_sampling(cfg, args, world, rank, local):
+    """A step = one tl_sample_tokens launch over B rows of logits (a new
+    uniform per step). value = tokens sampled per second."""
+    import torch
+    import tiny_llm_b200 as T
+    B, V = len(cfg["lens"]), cfg["vocab"]
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(args.seed * 7919 + rank)
+    lg = (torch.randn((B, V), device="cuda", generator=gen) * 3).half()
+    tok = torch.empty(B, dtype=torch.int32, device="cuda")
+    kw = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.9)
+
+    def step(i):
+        T.sample_tokens(lg.data_ptr(), V, B, V, tok.data_ptr(), seed=args.seed + rank, step=i, stream=sp, **kw)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    time.sleep(0.3)
+    barrier(world)
+    a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    z.record(stream)
+    z.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(z)
+    hl = torch.empty(lg.shape, dtype=torch.float16, pin_memory=True)
+    ht = torch.empty(tok.shape, dtype=torch.int32, pin_memory=True)
+    hl.copy_(lg.cpu())
+    torch.cuda.synchronize()
+    ea, ez = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for i in range(args.steps):
+        lg.copy_(hl, non_blocking=True)
+        step(i)
+        ht.copy_(tok, non_blocking=True)
+    ez.record(stream)
+    ez.synchronize()
+    e2e_ms = ea.elapsed_time(ez)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        import numpy as np
+        import oracle as O
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import sampling as S
+        rows = O.f16_to_f32(lg[:4].cpu().numpy().view(np.uint16)).astype(np.float64)
+        t0 = time.perf_counter()
+        for r in range(rows.shape[0]):
+            S.sample(rows[r], seed=args.seed, step=0, row=r, **kw)
+        el = time.perf_counter() - t0
+        cpu = {"value": round(rows.shape[0] / el, 2), "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": "4 rows through the oracle's float64 restatement of the reference's top-p sampler (numpy sort per row)"}
+    return dict(ms=ms, tokens=B * args.steps, e2e_ms=e2e_ms, h2d=hl.numel() * 2, d2h=ht.numel() * 4,
+                clocks=clocks, B=B, V=V, cpu=cpu, launches=args.steps)
+
+
 def run_reference_qkv(cfg, args, world, rank, local):
     """The reference's own decode-step projections and append, unchanged:
     three kernels::w8a16_matmul per layer into q/k/v buffers (given all B
@@ -1043,6 +1108,11 @@ def main():
         elif args.config == "pf":
             res, why = None, ("reference arm covers the decode configs; the reference prefill kernel "
                               "is compared in tests/test_gpu_reference.py")
+        elif args.config == "smp":
+            res, why = None, ("the reference samples on the host after a synchronize and a logits copy "
+                              "(src/inference_engine.cpp:296-307) inside its engine; its samplers are restated "
+                              "in oracle/sampling.py (the timed CPU baseline of our arm) and compared by "
+                              "tests/test_gpu_sampling.py")
         elif args.config == "qkv":
             res, why = run_reference_qkv(cfg, args, world, rank, local)
             if res is not None:
@@ -1135,6 +1205,38 @@ def main():
                                  if pk else "fallback"},
                     "cpu_baseline": None,
                     "e2e": {"value": round(fl / (e2e_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+                            "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
+                    "clocks": res["clocks"], "gpu_launches": res["launches"]}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    if args.config == "smp":
+        res = run_sampling(cfg, args, world, rank, local)
+        ms = barrier_max(res["ms"], world)
+        toks = barrier_sum(res["tokens"], world)
+        e2e_ms = barrier_max(res["e2e_ms"], world)
+        if rank == 0:
+            per = ms / args.steps
+            lbytes = res["B"] * res["V"] * 2
+            achieved = lbytes / (per / 1e3) / 1e9
+            line = {"metric": "next-token sampling tokens/s", "value": round(toks / (ms / 1e3), 1),
+                    "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": round(per, 4), "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "f16 logits (fp32 softmax mass)",
+                    "data": "synthetic N(0, 3) fp16 logits from a seeded generator",
+                    "config": {"workload": cfg["workload"], "rows": res["B"] * world, "vocab": res["V"],
+                               "strategy": "top-p 0.9, T 0.8 (do_sample)",
+                               "l2": "8 MB of logits, re-read per pass from L2 (one read from HBM)"},
+                    "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                 "frac": round(achieved / peak, 4), "traffic": None,
+                                 "kernel": "sample_kernel (one CTA per row, 6 passes over the row)",
+                                 "note": "32 CTAs on 148 SMs: one row per CTA bounds it by passes per row, not by HBM",
+                                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},
+                    "cpu_baseline": res["cpu"],
+                    "e2e": {"value": round(toks / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                             "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": res["d2h"]},
                     "clocks": res["clocks"], "gpu_launches": res["launches"]}
             print(json.dumps(line), flush=True)

@@ -220,6 +220,24 @@ int tl_project_qkv_append(tl_cache *cache, int layer, const void *x, int hidden,
                           const void *sq, const int8_t *wk, const void *sk, const int8_t *wv, const void *sv,
                           int group_size, const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream);
 
+/* Next-token sampling on the device for `rows` rows of fp16 logits
+ * (row_stride elements apart; 0 shares one row), replacing the host round
+ * trip of InferenceEngine::sampleFromHidden (reference
+ * src/inference_engine.cpp:296-307: stream synchronize, logits copied to the
+ * host, the host samplers of :330-490). The token ids go to tokens_out
+ * (device int32 [rows]); nothing is synchronised. Strategy as the
+ * reference's sample() (GenerationConfig, include/tiny_llm/types.h:96-102):
+ * do_sample == 0: greedy (first index of the largest logit); otherwise
+ * top_p < 1: top-p (p clamped to [1e-5, 1]); top_k > 0: top-k (k clamped to
+ * [1, vocab]); else temperature; T clamped to >= 1e-5. The draw is an
+ * inverse CDF over the candidates in descending logit order (ties by
+ * ascending index) with a uniform of (seed, step, row) from splitmix64: the
+ * same distribution as the reference's std::discrete_distribution, not the
+ * same draws. No handle: errors are read with tl_last_error(NULL). */
+int tl_sample_tokens(const void *logits, long long row_stride, int rows, int vocab, int do_sample,
+                     float temperature, int top_k, float top_p, unsigned long long seed, unsigned long long step,
+                     int *tokens_out, tl_stream_t stream);
+
 /* ---- Head-sharded decode across the GPUs of one node -------------------
  * No reference counterpart (the reference is single-GPU). With KV heads
  * split over `world` ranks (one process per GPU), each rank's decode writes

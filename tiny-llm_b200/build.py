@@ -30,7 +30,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter"]
 
-CU_SOURCES = ["kv_append.cu", "paged_decode.cu", "paged_prefill_tc.cu", "qkv_append.cu", "decode_static_scratch.cu"]
+CU_SOURCES = ["kv_append.cu", "paged_decode.cu", "paged_prefill_tc.cu", "qkv_append.cu", "sampling.cu", "decode_static_scratch.cu"]
 CPP_SOURCES = ["paged_kv.cpp", "kv_cache_manager.cpp"]
 HEADERS = ["kernels.h", "paged_kv.h", "ptx.cuh"]
 

@@ -178,6 +178,20 @@ struct QkvArgs {
     int row_pos[kMaxQkvRows];
 };
 
+// Token sampling, one CTA per row of logits.
+struct SampleArgs {
+    const void *logits;       // fp16 [rows] rows of `vocab`, row_stride elements apart
+    long long row_stride;
+    int rows, vocab;
+    int mode;                 // 0 greedy, 1 top-k (temperature: k = vocab), 2 top-p
+    float temperature;        // clamped (>= 1e-5)
+    int top_k;                // clamped to [1, vocab]
+    float top_p;              // clamped to [1e-5, 1]
+    unsigned long long seed, step;
+    int *tokens;              // device [rows]
+};
+cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s);
+
 int prefill_tc_rows_per_cta();
 cudaError_t launch_prefill_tc(const PrefillArgs &a, const void *tmap128, cudaStream_t s);
 int qkv_k_block();

@@ -1192,6 +1192,48 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
     return TL_OK;
 }
 
+// Token sampling on the device (reference src/inference_engine.cpp:296-307
+// and the samplers of :330-490). No handle: errors are read back with
+// tl_last_error(NULL).
+int tl_sample_tokens(const void *logits, long long row_stride, int rows, int vocab, int do_sample,
+                     float temperature, int top_k, float top_p, unsigned long long seed, unsigned long long step,
+                     int *tokens_out, tl_stream_t stream) {
+    auto fail = [](int st, const std::string &m) {
+        g_create_error = m;
+        return st;
+    };
+    if (rows < 0 || vocab <= 0) return fail(TL_ERR_INVALID_ARG, "sampleTokens: rows must be >= 0 and vocab > 0");
+    if (rows == 0) return TL_OK;
+    if (!logits || !tokens_out)
+        return fail(TL_ERR_INVALID_ARG, !logits ? "sampleTokens: logits is null" : "sampleTokens: tokens is null");
+    if (rows > 1 && row_stride < vocab && row_stride != 0)
+        return fail(TL_ERR_INVALID_ARG, "sampleTokens: row_stride must be 0 (shared logits) or >= vocab");
+    tllm::SampleArgs a{};
+    a.logits = logits;
+    a.row_stride = row_stride;
+    a.rows = rows;
+    a.vocab = vocab;
+    a.temperature = std::max(temperature, 1e-5f);  // as the reference clamps
+    a.seed = seed;
+    a.step = step;
+    a.tokens = tokens_out;
+    if (!do_sample) {
+        a.mode = 0;
+    } else if (top_p < 1.0f) {
+        a.mode = 2;
+        a.top_p = std::min(std::max(top_p, 1e-5f), 1.0f);
+    } else {
+        a.mode = 1;
+        a.top_k = top_k > 0 ? std::max(1, std::min(top_k, vocab)) : vocab;  // temperature: every token
+    }
+    cudaError_t e = tllm::launch_sample(a, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(TL_ERR_CUDA, std::string("sampleTokens: launch failed: ") + cudaGetErrorString(e));
+    }
+    return TL_OK;
+}
+
 int tl_peer_init(tl_cache *c, int rank, int world, size_t gather_bytes, void *ipc_handle) {
     if (!c) return TL_ERR_INVALID_ARG;
     if (world < 1 || world > tllm::kMaxPeers || rank < 0 || rank >= world || !ipc_handle)

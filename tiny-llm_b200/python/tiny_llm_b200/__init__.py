@@ -44,7 +44,7 @@ EXPORTED_SYMBOLS = [
     "tl_permute_free_blocks", "tl_debug_inject_alloc_failure", "tl_version",
     "tl_decode_attention_static", "tl_peer_init", "tl_peer_connect", "tl_peer_buffer",
     "tl_decode_attention_peer", "tl_attention_step", "tl_prefill_attention",
-    "tl_project_qkv_append",
+    "tl_project_qkv_append", "tl_sample_tokens",
 ]
 
 
@@ -144,6 +144,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_attention_step": (i, [vp, i, vp, vp, vp, vp, ip, i, f, vp]),
         "tl_prefill_attention": (i, [vp, i, vp, vp, ip, ip, i, f, vp]),
         "tl_project_qkv_append": (i, [vp, i, vp, i, vp, vp, vp, vp, vp, vp, i, ip, i, vp, vp]),
+        "tl_sample_tokens": (i, [vp, ll, i, i, i, f, i, f, C.c_ulonglong, C.c_ulonglong, vp, vp]),
         "tl_sync_check": (i, [vp, vp]),
         "tl_rope_table": (None, [C.POINTER(C.c_float), C.POINTER(C.c_float), i, i, f]),
         "tl_permute_free_blocks": (i, [vp, C.c_ulonglong]),
@@ -372,6 +373,19 @@ def decode_attention_static(view: PagedView, layer, q_ptr, o_ptr, table_rows, se
                                         stream or None, buf, 512)
     if st != TL_OK:
         raise _ERRORS.get(st, TLError)(st, buf.value.decode())
+
+
+def sample_tokens(logits_ptr, row_stride, rows, vocab, tokens_ptr, do_sample=False, temperature=1.0, top_k=50,
+                  top_p=0.9, seed=0, step=0, stream=0):
+    """tl_sample_tokens: one next token per row of fp16 logits, left in device
+    memory (defaults as the reference's GenerationConfig: greedy unless
+    do_sample; then top_p < 1, top_k > 0, or temperature)."""
+    lib = load()
+    st = lib.tl_sample_tokens(logits_ptr, int(row_stride), int(rows), int(vocab), int(bool(do_sample)),
+                              float(temperature), int(top_k), float(top_p), int(seed) & (2**64 - 1),
+                              int(step) & (2**64 - 1), tokens_ptr, stream or None)
+    if st != TL_OK:
+        raise _ERRORS.get(st, TLError)(st, lib.tl_last_error(None).decode())
 
 
 def inject_alloc_failure(nth: int) -> None:
