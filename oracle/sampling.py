@@ -127,7 +127,7 @@ def window(logits, do_sample=True, temperature=1.0, top_k=50, top_p=0.9, seed=0,
         order = np.lexsort((np.arange(x.size), -np.where(valid, x, -np.inf)))
         c = np.cumsum(allw[order]) / allw.sum()
         p = min(max(float(np.float32(top_p)), 1e-5), 1.0)
-        near = np.nonzero(np.abs(c - p) < tol)[0]
+        near = np.nonzero(np.abs(c - p) < tol)[0][:4]
         for i in near:  # a cutoff that float32 sums could also pick
             sets.append((order[:i + 1], allw[order[:i + 1]]))
             sets.append((order[:min(i + 2, x.size)], allw[order[:min(i + 2, x.size)]]))
@@ -138,8 +138,6 @@ def window(logits, do_sample=True, temperature=1.0, top_k=50, top_p=0.9, seed=0,
         if not total > 0:
             continue
         cum = np.concatenate(([0.0], np.cumsum(ws))) / total
-        lo, hi = u - tol, u + tol
-        for j in range(len(ids)):
-            if cum[j + 1] > lo and cum[j] <= hi:
-                out.add(int(ids[j]))
+        hit = (cum[1:] > u - tol) & (cum[:-1] <= u + tol)
+        out.update(int(i) for i in np.asarray(ids)[hit])
     return out
