@@ -32,6 +32,7 @@
 // accumulator, rounds to fp16 like the reference's output, rotates Q and K
 // pairs (d, d + D/2) by the RoPE table at the row's position exactly as the
 // append kernel does, and writes Q to q_out and K/V into the pool.
+#include <atomic>
 #include <cstdint>
 #include <cuda_fp16.h>
 
@@ -307,13 +308,14 @@ cudaError_t launch_mt(const QkvArgs &a, cudaStream_t s) {
     cudaError_t e = cudaSuccess;
     auto go = [&](auto kern) {
         // the shared-memory opt-in, raised only when a launch needs more
-        // than the last one set (per device)
-        static int opted[64] = {};
+        // than the last one set (per device; host threads may race to set
+        // it, which is harmless)
+        static std::atomic<int> opted[64];
         int dev = 0;
         e = cudaGetDevice(&dev);
-        if (e == cudaSuccess && (dev >= 64 || opted[dev] < smem)) {
+        if (e == cudaSuccess && (dev >= 64 || opted[dev].load(std::memory_order_relaxed) < smem)) {
             e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (e == cudaSuccess && dev < 64) opted[dev] = smem;
+            if (e == cudaSuccess && dev < 64) opted[dev].store(smem, std::memory_order_relaxed);
         }
         if (e == cudaSuccess) {
             kern<<<grid, D, smem, s>>>(a);
