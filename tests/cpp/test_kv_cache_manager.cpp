@@ -4,6 +4,7 @@
 // every test runs on the bookkeeping backend (no device needed) and the data
 // round trip is skipped; with --gpu the CUDA backend is used throughout.
 #include <algorithm>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <functional>
@@ -188,6 +189,29 @@ int main(int argc, char **argv) {
         EXPECT(cache->getSeqLen(id) == 0);
         EXPECT(cache->advanceSeqLen(id, n).isOk());
         EXPECT(cache->getSeqLen(id) == n);
+    });
+    run("ProjectQKVAppendValidatesArguments", [] {  // the decode step's Q/K/V projection + append
+        // every case here is refused before any device work (safe with --gpu)
+        auto cache = createCache(createConfig(2, 4, 64, 32, 2));
+        int id = cache->allocateSequence(2).value();
+        auto H = [](uintptr_t a) { return reinterpret_cast<const half *>(a); };
+        const int8_t *w = reinterpret_cast<const int8_t *>(uintptr_t(256));
+        half *q = reinterpret_cast<half *>(uintptr_t(256));
+        auto call = [&](int layer, const half *x, int hidden, const half *sk, int group, std::vector<int> ids) {
+            return cache->projectQKVAppend(layer, x, hidden, w, H(256), w, sk, w, H(256), group, ids, q);
+        };
+        auto has = [](const Result<void> &r, const char *s) {
+            return r.isErr() && r.error().find(s) != std::string::npos;
+        };
+        EXPECT(has(call(2, H(256), 256, H(256), 32, {id}), "Invalid layer_idx"));
+        EXPECT(has(call(0, nullptr, 256, H(256), 32, {id}), "input is null"));
+        EXPECT(has(call(0, H(256), 200, H(256), 32, {id}), "supported shapes"));
+        EXPECT(has(call(0, H(256), 256, H(256), 8, {id}), "supported shapes"));
+        EXPECT(has(call(0, H(256), 256, H(258), 32, {id}), "aligned"));
+        EXPECT(has(call(0, H(256), 256, H(256), 32, {id + 7}), "not found"));
+        EXPECT(has(call(0, H(256), 256, H(256), 32, {id, id}), "duplicate"));
+        if (!g_gpu) EXPECT(has(call(0, H(256), 256, H(256), 32, {id}), "no CUDA device"));
+        EXPECT(cache->getSeqLen(id) == 0);
     });
     if (g_gpu) {
         run("KVCacheAppendRetrieve", [] {  // tests/test_transformer.cu:141-194
