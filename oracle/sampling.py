@@ -112,8 +112,9 @@ def sample(logits, do_sample=False, temperature=1.0, top_k=50, top_p=0.9, seed=0
 def window(logits, do_sample=True, temperature=1.0, top_k=50, top_p=0.9, seed=0, step=0, row=0, tol=1e-4):
     """The tokens a float32 implementation of the same draw may return: those
     whose CDF interval meets [target - tol, target + tol] (as fractions of
-    the total), over both candidate sets when the top-p cutoff itself lies
-    within tol of p."""
+    the total), over the oracle's candidate set and, for top-p, the cutoffs
+    up to two tokens either side of it whose cumulative mass is within tol
+    of p."""
     x = np.asarray(logits, dtype=np.float64)
     if mode_of(do_sample, top_k, top_p) == "greedy" or x.size == 0:
         return {greedy(x)}
@@ -127,10 +128,10 @@ def window(logits, do_sample=True, temperature=1.0, top_k=50, top_p=0.9, seed=0,
         order = np.lexsort((np.arange(x.size), -np.where(valid, x, -np.inf)))
         c = np.cumsum(allw[order]) / allw.sum()
         p = min(max(float(np.float32(top_p)), 1e-5), 1.0)
-        near = np.nonzero(np.abs(c - p) < tol)[0][:4]
-        for i in near:  # a cutoff that float32 sums could also pick
-            sets.append((order[:i + 1], allw[order[:i + 1]]))
-            sets.append((order[:min(i + 2, x.size)], allw[order[:min(i + 2, x.size)]]))
+        cut = len(idx)
+        for n in range(max(1, cut - 2), min(cut + 2, x.size) + 1):  # cutoffs float32 sums could pick
+            if n != cut and abs(c[n - 1] - p) < tol:
+                sets.append((order[:n], allw[order[:n]]))
     u = uniform(seed, step, row)
     out = set()
     for ids, ws in sets:
