@@ -256,6 +256,18 @@ int tl_peer_init(tl_cache *cache, int rank, int world, size_t gather_bytes, void
 int tl_peer_connect(tl_cache *cache, const void *ipc_handles);
 /* Device address and size of this rank's gathered-output area. */
 int tl_peer_buffer(const tl_cache *cache, void **gathered, size_t *bytes);
+/* Limit, in seconds, of each wait for a peer's flag in later
+ * tl_decode_attention_peer calls (<= 0: the built-in 10 s; at most 600). A
+ * wait that runs out stops the gather, leaves the other ranks' slices
+ * unwritten and is reported by tl_sync_check as TL_ERR_DEVICE_FAULT ("bounded
+ * wait timed out"); the handle stays usable. No reference counterpart. */
+int tl_set_peer_wait_limit(tl_cache *cache, double seconds);
+/* Testing hook: uses `region`, device memory of this process laid out as a
+ * peer region ([flags 256 B][gathered outputs], 256-byte aligned), as rank
+ * `rank`'s region instead of an IPC mapping, so the publish/pull protocol
+ * (and a peer that never publishes) can be exercised on one GPU. Once every
+ * rank of the world has a region the handle counts as connected. */
+int tl_debug_peer_attach(tl_cache *cache, int rank, void *region);
 /* tl_decode_attention for this rank's heads, all ranks calling it for the
  * same layer with the same out_offset, num_seqs and `epoch` (a value that
  * increases call to call). This rank's [num_seqs][Hq][D] slice lands at
@@ -270,14 +282,15 @@ int tl_decode_attention_peer(tl_cache *cache, int layer, const void *q, const in
 /* A paged KV pool that lives in memory the caller owns, laid out as the
  * handle's pool: fp16 [num_layers][2 (K,V)][num_blocks][block], each block
  * [block_size][Hkv][D] (token-major) or [Hkv][block_size][D] (head-major);
- * block_tables is int32 [rows][bt_stride] on the device, entry j of a row
- * being the block that holds tokens j*block_size .. j*block_size+bs-1. */
+ * block_tables is int32 [num_rows][bt_stride] on the device, entry j of a
+ * row being the block that holds tokens j*block_size .. j*block_size+bs-1. */
 typedef struct {
     void *pool;
     const int *block_tables;
     int *error_word;      /* optional device int: kernels OR error bits into it */
     long long num_blocks;
     int num_layers, num_kv_heads, num_q_heads, head_dim, block_size, layout, bt_stride;
+    int num_rows;         /* rows of block_tables; every table row used must be below it */
 } tl_paged_view;
 
 /* Decode attention that allocates nothing. No counterpart in the reference:
@@ -286,8 +299,8 @@ typedef struct {
  * allocator, or a path that must not risk the implicit device
  * synchronisation of cudaMalloc/cudaFree. Everything is the caller's:
  * the pool and block tables (`view`), q/o ([num_seqs][Hq][D] fp16, device),
- * and, on the host, table_rows[i] (the block-table row of sequence i) and
- * seq_lens[i] (tokens it attends). The math and output are those of
+ * and, on the host, table_rows[i] (the block-table row of sequence i, in
+ * 0..num_rows-1) and seq_lens[i] (tokens it attends). The math and output are those of
  * tl_decode_attention. The split-K scratch is a file-scope device array of
  * 8 MiB inside this library, present on every GPU that loads it until the
  * process exits; num_seqs above 256, or a shape whose split partials cannot

@@ -2,9 +2,9 @@
 own CUDA code (oracle/_ref/libtllm_ref.so, built from the reference sources
 by oracle/Makefile.ref) on seeded inputs. Needs a GPU; run on the GPU box:
 
-    python tests/golden/make_golden.py <out_dir>
+    python tests/golden/make_golden.py [out_dir]
 
-and copy <out_dir>/*.npz into tests/golden/. Inputs are regenerated from
+which writes the *.npz files to out_dir (default: tests/golden/ itself). Inputs are regenerated from
 their seeds by the oracle's generator (oracle.normal_f16); each fixture stores
 the seeds, shapes, a SHA-256 of the generated inputs (to catch generator
 drift) and the reference's outputs.
@@ -112,4 +112,5 @@ def main(out: Path):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "gpurun_out/golden"))
+    # output directory: the first argument, else the fixtures' own directory
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent)

@@ -1,4 +1,5 @@
-"""Parity at the BASELINE configs' full sizes (c2, c3, c4 on one GPU).
+"""Parity at the BASELINE configs' full sizes (c2, c3, c4 on one GPU, and
+config 5's steady-state batch of 225 short sequences).
 
 The whole batch is prefilled through the per-layer append (RoPE on K), one
 fused all-layer append step is applied, and decode runs on the sampled layers
@@ -26,7 +27,16 @@ CASES = {
     "c2": (32, 32, 32, 128, 16, [2048] * 32, False),
     "c3": (32, 32, 8, 128, 16, "ragged", True),
     "c4": (80, 64, 8, 128, 32, [32768] * 8, False),
+    # config 5's steady-state decode batch: 225 sequences, log-uniform
+    # prompts in [32, 4096] plus half a geometric(256) generation, permuted
+    "c5s": (32, 32, 8, 128, 16, "loguniform", True),
 }
+
+
+def _loguniform_lens(seed=0, n=225, lo=32, hi=4096):
+    rng = np.random.default_rng(seed)
+    return [int(round(math.exp(x))) + int(rng.geometric(1 / 256)) // 2
+            for x in rng.uniform(math.log(lo), math.log(hi), size=n)]
 
 
 def _kv_chunk(torch, sid, layer, P, Hkv, D):
@@ -44,6 +54,8 @@ def test_full_size_config(name):
     L, Hq, Hkv, D, bs, lens, permute = CASES[name]
     if lens == "ragged":
         lens = [int(x) for x in np.random.default_rng(0).integers(512, 8193, size=64)]
+    elif lens == "loguniform":
+        lens = _loguniform_lens()
     B = len(lens)
     max_len = max(lens) + 4
     nblocks = sum(-(-(l + 4) // bs) for l in lens)
@@ -64,7 +76,8 @@ def test_full_size_config(name):
     cache.sync_check()
 
     rng = np.random.default_rng(1)
-    sample = sorted({(int(rng.integers(B)), int(rng.integers(L))) for _ in range(3)})
+    nsample = 8 if B > 100 else 3  # many short sequences: sample more of them
+    sample = sorted({(int(rng.integers(B)), int(rng.integers(L))) for _ in range(nsample)})
     cos, sin = O.rope_table(max_len, D, 10000.0)
     base, _ = cache.pool()
     cfg = cache.config

@@ -93,3 +93,34 @@ def test_distribution_over_rows():
     p /= p.sum()
     f = np.bincount(got, minlength=V) / rows
     assert np.all(np.abs(f - p) <= 5 * np.sqrt(p * (1 - p) / rows) + 1e-3)
+
+
+@pytest.mark.parametrize("kw", [
+    dict(temperature=0.5, top_k=1000, top_p=1.0),    # the k-th largest inside 5000 ties
+    dict(temperature=0.01, top_k=0, top_p=0.5),      # 3000 tied maxima, half the mass
+    dict(temperature=0.02, top_k=0, top_p=0.97),     # cutoff inside the second tie group
+])
+def test_draws_with_many_ties_at_the_cutoff(kw):
+    """Thousands of equal logits at the candidate cutoff under low
+    temperature: the drawn index among the ties (ascending) must be the
+    oracle's, never the pre-set argmax standing in for it."""
+    rows, V = 64, 32000
+    rng = np.random.default_rng(5)
+    x = rng.normal(0, 1, (rows, V)).astype(np.float32) - 8.0
+    if kw["top_k"]:
+        x[:, rng.choice(V, 10, replace=False)] = 5.0
+        x[:, rng.choice(V, 5000, replace=False)] = 4.75
+    else:
+        top = rng.choice(V, 6000, replace=False)
+        x[:, top[:3000]] = 5.0
+        x[:, top[3000:]] = 4.96875
+    lg = O.f32_to_f16(x)
+    seed, step = 77, 3
+    got = _run(lg, rows, V, V, do_sample=True, seed=seed, step=step, **kw)
+    argmax_hits = 0
+    for r in range(rows):
+        xr = O.f16_to_f32(lg[r]).astype(np.float64)
+        ok = S.window(xr, True, seed=seed, step=step, row=r, tol=1e-4, **kw)
+        assert int(got[r]) in ok, f"row {r}: {got[r]} not in {sorted(ok)[:8]}"
+        argmax_hits += int(got[r]) == S.greedy(xr)
+    assert argmax_hits < rows // 2

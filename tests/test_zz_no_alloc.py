@@ -7,8 +7,9 @@ cudaMalloc/cudaFree. It reads a pool and block tables the caller owns and
 keeps its split-K scratch in a fixed array inside the library, which every
 call reuses. So this test makes two calls in a row with different layers
 and queries (the second call starts with the first one's scratch contents)
-and checks each against the handle-based entry point on the same pool,
-within the attention tolerance of the other parity tests.
+and checks each against the handle-based entry point on the same pool and
+against the CPU oracle's attention over the same logical K/V, within the
+attention tolerance of the other parity tests.
 
 The file name makes pytest collect it last, so a run that stops at the first
 failure has already run every other test.
@@ -51,13 +52,15 @@ def test_static_scratch_decode_matches_handle_decode_on_two_calls():
     cfg = cache.config
     view = T.PagedView(pool=base, block_tables=bt_dev.data_ptr(), error_word=err.data_ptr(),
                        num_blocks=cfg.num_blocks, num_layers=L, num_kv_heads=Hkv, num_q_heads=Hq,
-                       head_dim=D, block_size=bs, layout=cfg.layout, bt_stride=stride)
+                       head_dim=D, block_size=bs, layout=cfg.layout, bt_stride=stride,
+                       num_rows=len(sids))
     rows = list(range(len(sids)))
     seq_lens = [cache.get_seq_len(s) for s in sids]
     assert seq_lens == lens
 
     for call, layer in enumerate([0, 1]):
-        q = to_dev(O.normal_f16((len(sids), Hq, D), 100 + call))
+        qh = O.normal_f16((len(sids), Hq, D), 100 + call)
+        q = to_dev(qh)
         o_ref = torch.full((len(sids), Hq, D), 0x7e00, dtype=torch.int16, device="cuda")
         cache.decode_attention(layer, q.data_ptr(), o_ref.data_ptr(), sids)
         cache.sync_check()
@@ -69,6 +72,13 @@ def test_static_scratch_decode_matches_handle_decode_on_two_calls():
         got = O.f16_to_f32(from_dev(o))
         assert np.isfinite(got).all()
         check_close(got, ref, f"static-scratch call {call + 1} (layer {layer})")
+        for i, sid in enumerate(sids):  # and against the oracle directly
+            lk, lv = r.logical_k[(sid, layer)], r.logical_v[(sid, layer)]
+            if not lk:
+                assert not got[i].any(), "a sequence with no tokens must give zeros"
+                continue
+            want = O.decode_one(qh[i], np.stack(lk), np.stack(lv), 1.0 / np.sqrt(D))
+            check_close(got[i], want, f"static-scratch call {call + 1} seq {i} vs oracle")
 
 
 def test_static_scratch_rejects_oversized_requests():
@@ -76,10 +86,13 @@ def test_static_scratch_rejects_oversized_requests():
         pytest.skip("no CUDA device")
     view = T.PagedView(pool=16, block_tables=16, error_word=None, num_blocks=4, num_layers=1,
                        num_kv_heads=1, num_q_heads=1, head_dim=128, block_size=16, layout=0,
-                       bt_stride=1)
+                       bt_stride=1, num_rows=2)
     with pytest.raises(T.InvalidArgument) as e:
         T.decode_attention_static(view, 0, 16, 16, list(range(300)), [1] * 300)
     assert "num_seqs" in str(e.value)
+    with pytest.raises(T.InvalidArgument) as e:  # a table row past the caller's table
+        T.decode_attention_static(view, 0, 16, 16, [2], [1])
+    assert "table row" in str(e.value)
     with pytest.raises(T.Unsupported):
         view.head_dim = 96
         T.decode_attention_static(view, 0, 16, 16, [0], [1])

@@ -98,11 +98,11 @@ extern "C" int tl_decode_attention_static(const tl_paged_view *view, int layer, 
     const int D = v.head_dim, Hkv = v.num_kv_heads, Hq = v.num_q_heads, bs = v.block_size;
     if (!(D == 64 || D == 128 || D == 256) || !(bs == 16 || bs == 32) || Hkv <= 0 || Hq <= 0 ||
         Hq % Hkv != 0 || Hq / Hkv > 8 || v.num_layers <= 0 || v.num_blocks <= 0 ||
-        v.bt_stride <= 0 ||
+        v.bt_stride <= 0 || v.num_rows <= 0 ||
         (v.layout != TL_LAYOUT_TOKEN_MAJOR && v.layout != TL_LAYOUT_HEAD_MAJOR))
         return ret(fail(TL_ERR_UNSUPPORTED,
                         "decodeAttentionStatic: supported shapes are head_dim 64/128/256, "
-                        "block_size 16/32, query group 1..8, a valid layout"));
+                        "block_size 16/32, query group 1..8, a valid layout, num_rows > 0"));
     if (layer < 0 || layer >= v.num_layers)
         return ret(fail(TL_ERR_INVALID_ARG, "decodeAttentionStatic: Invalid layer_idx: " +
                                                 std::to_string(layer)));
@@ -160,10 +160,12 @@ extern "C" int tl_decode_attention_static(const tl_paged_view *view, int layer, 
     const long long row = (long long)Hq * D;
     for (int i = 0; i < num_seqs; ++i) {
         const int S = seq_lens[i];
-        if (S < 0 || (long long)S > (long long)v.bt_stride * bs || table_rows[i] < 0)
+        if (S < 0 || (long long)S > (long long)v.bt_stride * bs || table_rows[i] < 0 ||
+            table_rows[i] >= v.num_rows)
             return ret(fail(TL_ERR_INVALID_ARG,
                             "decodeAttentionStatic: sequence " + std::to_string(i) +
-                                " has a length outside 0..bt_stride*block_size or a negative table row"));
+                                " has a length outside 0..bt_stride*block_size or a table row outside "
+                                "0..num_rows-1"));
         a.slot[i] = table_rows[i];
         a.len[i] = S;
         a.prefix[i + 1] = a.prefix[i] + tllm::unit_slots((S + tllm::kDecodeTile - 1) / tllm::kDecodeTile);

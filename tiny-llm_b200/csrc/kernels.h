@@ -103,6 +103,7 @@ struct DecodeArgs {
     const unsigned char *peer_base[kMaxPeers];
     int world, rank;
     unsigned long long gather_off, slice_bytes;
+    unsigned long long peer_wait_ns;  // limit of each peer-flag wait; 0 -> the built-in 10 s
     int layer;
     int group;              // G = Hq / Hkv
     float scale_log2;       // softmax scale * log2(e)

@@ -163,12 +163,13 @@ __device__ void pull_peer_slices(const DecodeArgs &a) {
         int ok = 1;
         if (r < a.world && r != a.rank) {
             const unsigned *flag = reinterpret_cast<const unsigned *>(a.peer_base[r]) + r;
+            const uint64_t limit = a.peer_wait_ns ? a.peer_wait_ns : kPeerWaitLimitNs;
             const uint64_t t0 = ptx::globaltimer_ns();
             for (;;) {
                 unsigned v;
                 asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
                 if ((int)(v - a.epoch) >= 0) break;
-                if (ptx::globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+                if (ptx::globaltimer_ns() - t0 > limit) {
                     atomicOr(a.g.err, kErrWaitTimeout);
                     ok = 0;
                     break;
@@ -931,15 +932,17 @@ cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s) {
 }
 
 cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
+    // resolved once, by a thread-safe static initialiser (first calls may
+    // come from several host threads at once)
+    static const PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
         cudaDriverEntryPointQueryResult q;
         void *fn = nullptr;
         cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
                                                          cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess) fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }();
+    if (!encode) return cudaErrorNotSupported;
     const unsigned long long L2 = 2ull * g.num_layers;
     cuuint64_t dims[3], strides[2];
     cuuint32_t box[3], estr[3] = {1, 1, 1};

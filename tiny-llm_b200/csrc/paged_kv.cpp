@@ -867,6 +867,7 @@ int decode_impl(tl_cache *c, const char *ctx, int layer, const void *q, void *o,
             a.rank = c->peer_rank;
             a.gather_off = tllm::kPeerFlagBytes + peer->out_offset;
             a.slice_bytes = slice;
+            a.peer_wait_ns = c->peer_wait_ns;
         }
         a.prefix[0] = 0;
         for (int i = 0; i < n; ++i) {
@@ -1289,6 +1290,36 @@ int tl_peer_connect(tl_cache *c, const void *ipc_handles) {
         c->peer_opened[r] = true;
     }
     c->peers_connected = true;
+    return TL_OK;
+}
+
+int tl_set_peer_wait_limit(tl_cache *c, double seconds) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    if (!(seconds <= 600.0))
+        return set_error(c, TL_ERR_INVALID_ARG, "setPeerWaitLimit: seconds must be at most 600 (<= 0: default)");
+    c->peer_wait_ns = seconds > 0.0 ? (unsigned long long)(seconds * 1e9) : 0ull;
+    if (seconds > 0.0 && c->peer_wait_ns == 0) c->peer_wait_ns = 1;
+    return TL_OK;
+}
+
+int tl_debug_peer_attach(tl_cache *c, int rank, void *region) {
+    if (!c) return TL_ERR_INVALID_ARG;
+    if (!c->peer_region)
+        return set_error(c, TL_ERR_INVALID_ARG, "peerAttach: call tl_peer_init first");
+    if (rank < 0 || rank >= c->peer_world || rank == c->peer_rank || !region ||
+        ((uintptr_t)region & 255u))
+        return set_error(c, TL_ERR_INVALID_ARG,
+                         "peerAttach: need another rank of the world and a 256-byte aligned region");
+    if (c->peer_opened[rank]) {
+        DeviceGuard guard(c);
+        cudaIpcCloseMemHandle(c->peer_bases[rank]);
+        c->peer_opened[rank] = false;
+    }
+    c->peer_bases[rank] = region;
+    c->peer_bases[c->peer_rank] = c->peer_region;
+    bool all = true;
+    for (int r = 0; r < c->peer_world; ++r) all = all && c->peer_bases[r] != nullptr;
+    c->peers_connected = all;
     return TL_OK;
 }
 

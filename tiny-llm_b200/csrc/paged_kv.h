@@ -85,6 +85,7 @@ struct tl_cache {
     void *peer_bases[tllm::kMaxPeers] = {};
     bool peer_opened[tllm::kMaxPeers] = {};
     bool peers_connected = false;
+    unsigned long long peer_wait_ns = 0;  // 0: the kernel's built-in limit (10 s)
     size_t partial_floats = 0;
     // fused Q/K/V projection + append: split-K partials and per-tile counters
     float *qkv_partial = nullptr;

@@ -33,6 +33,8 @@
 // pairs (d, d + D/2) by the RoPE table at the row's position exactly as the
 // append kernel does, and writes Q to q_out and K/V into the pool.
 #include <atomic>
+#include <map>
+#include <mutex>
 #include <cstdint>
 #include <cuda_fp16.h>
 
@@ -307,15 +309,21 @@ cudaError_t launch_mt(const QkvArgs &a, cudaStream_t s) {
     const dim3 grid(a.ksplit, a.num_q_heads + 2 * a.g.num_kv_heads);
     cudaError_t e = cudaSuccess;
     auto go = [&](auto kern) {
-        // the shared-memory opt-in, raised only when a launch needs more
-        // than the last one set (per device; host threads may race to set
-        // it, which is harmless)
-        static std::atomic<int> opted[64];
+        // the shared-memory opt-in of this kernel on this device, only ever
+        // raised; the check, the set and the record happen under one lock so
+        // host threads launching different chunk sizes cannot leave the
+        // record above the attribute
+        static std::mutex mu;
+        static std::map<std::pair<int, const void *>, int> opted;  // (device, kernel) -> bytes
         int dev = 0;
         e = cudaGetDevice(&dev);
-        if (e == cudaSuccess && (dev >= 64 || opted[dev].load(std::memory_order_relaxed) < smem)) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (e == cudaSuccess && dev < 64) opted[dev].store(smem, std::memory_order_relaxed);
+        if (e == cudaSuccess) {
+            std::lock_guard<std::mutex> lock(mu);
+            int &cur = opted[{dev, reinterpret_cast<const void *>(kern)}];
+            if (cur < smem) {
+                e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                if (e == cudaSuccess) cur = smem;
+            }
         }
         if (e == cudaSuccess) {
             kern<<<grid, D, smem, s>>>(a);

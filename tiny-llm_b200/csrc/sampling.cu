@@ -321,6 +321,9 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __grid_con
         wsum[lane] = w;  // inclusive over warps
     }
     __syncthreads();
+    // j never passes the last index holding ks (wsum[31] of them): rounding
+    // in the mass walk cannot leave the pre-set argmax standing in for a draw
+    j = min(j, wsum[31] - 1);
     const int excl = incl - cnt + (warp > 0 ? wsum[warp - 1] : 0);
     if (j >= excl && j < excl + cnt) {
         int seen = excl;

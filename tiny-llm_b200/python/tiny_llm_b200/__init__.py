@@ -44,7 +44,7 @@ EXPORTED_SYMBOLS = [
     "tl_permute_free_blocks", "tl_debug_inject_alloc_failure", "tl_version",
     "tl_decode_attention_static", "tl_peer_init", "tl_peer_connect", "tl_peer_buffer",
     "tl_decode_attention_peer", "tl_attention_step", "tl_prefill_attention",
-    "tl_project_qkv_append", "tl_sample_tokens",
+    "tl_project_qkv_append", "tl_sample_tokens", "tl_set_peer_wait_limit", "tl_debug_peer_attach",
 ]
 
 
@@ -88,7 +88,7 @@ class PagedView(C.Structure):
         ("pool", C.c_void_p), ("block_tables", C.c_void_p), ("error_word", C.c_void_p),
         ("num_blocks", C.c_longlong), ("num_layers", C.c_int), ("num_kv_heads", C.c_int),
         ("num_q_heads", C.c_int), ("head_dim", C.c_int), ("block_size", C.c_int),
-        ("layout", C.c_int), ("bt_stride", C.c_int),
+        ("layout", C.c_int), ("bt_stride", C.c_int), ("num_rows", C.c_int),
     ]
 
 
@@ -156,6 +156,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_peer_connect": (i, [vp, vp]),
         "tl_peer_buffer": (i, [vp, C.POINTER(vp), C.POINTER(sz)]),
         "tl_decode_attention_peer": (i, [vp, i, vp, ip, i, f, sz, C.c_uint, vp]),
+        "tl_set_peer_wait_limit": (i, [vp, C.c_double]),
+        "tl_debug_peer_attach": (i, [vp, i, vp]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
@@ -339,6 +341,15 @@ class KVCache:
         p, n = C.c_void_p(), C.c_size_t()
         self._check(self._lib.tl_peer_buffer(self._h, C.byref(p), C.byref(n)))
         return p.value, n.value
+
+    def set_peer_wait_limit(self, seconds: float) -> None:
+        """Limit of each wait for a peer's flag (<= 0: the built-in 10 s)."""
+        self._check(self._lib.tl_set_peer_wait_limit(self._h, float(seconds)))
+
+    def debug_peer_attach(self, rank: int, region_ptr: int) -> None:
+        """Testing hook: a local device region stands in for rank `rank`'s
+        IPC-shared peer region (one-GPU tests of the gather protocol)."""
+        self._check(self._lib.tl_debug_peer_attach(self._h, int(rank), region_ptr))
 
     def decode_attention_peer(self, layer, q_ptr, seq_ids, out_offset, epoch, scale=0.0, stream=0):
         self._check(self._lib.tl_decode_attention_peer(self._h, int(layer), q_ptr, _ids(seq_ids),
