@@ -23,9 +23,13 @@ block 16, RoPE theta 10000 on K at append. KV bytes read per step ~34.4 GB
 --impl reference runs the reference's own path instead (oracle/_ref:
 KVCacheManager::appendKV + kernels::attention_decode, rebuilt for sm_100a).
 
-Multi-GPU (torchrun): each rank runs the same per-GPU batch on its own GPU
-(batch sharding: independent sequences, no data-path collective), so the
-scaling is weak; time is the max over ranks.
+Multi-GPU (torchrun): by default the config's own batch of sequences is
+split over the ranks, balanced by KV bytes (dist.batch_shard: independent
+sequences, no data-path collective), so the total work is fixed and the
+scaling is strong; --scaling weak gives every rank the whole batch instead.
+--shard head splits the KV heads of every sequence over the ranks and
+gathers each layer's outputs. Time is the max over ranks; the line also
+lists every rank's time.
 """
 from __future__ import annotations
 
@@ -203,6 +207,33 @@ def barrier_sum(value: float, world: int) -> float:
     return float(t.item())
 
 
+def gather_values(value: float, world: int) -> list[float]:
+    """Every rank's value of a host scalar, in rank order."""
+    if world == 1:
+        return [value]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
+def rank_lens(cfg, args, world, rank):
+    """(sequence lengths this rank decodes, global batch). Strong scaling
+    (the default): the config's own batch split over the ranks, balanced by
+    KV bytes (dist.batch_shard); weak: every rank runs a whole batch."""
+    if world == 1 or args.scaling == "weak":
+        lens = seq_lens(cfg, args.seed, rank)
+        return lens, len(lens) * world
+    from tiny_llm_b200 import dist as TD
+    all_lens = seq_lens(cfg, args.seed, 0)
+    mine = TD.batch_shard(all_lens, world)[rank]
+    if not mine:
+        raise SystemExit(f"{len(all_lens)} sequences do not give every one of {world} ranks a sequence")
+    return [all_lens[i] for i in mine], len(all_lens)
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -229,8 +260,9 @@ def run_ours(cfg, args, world, rank, local):
         sl = TD.head_shard(Hkv, Hq, world, rank)
         Hkv, Hq = sl.kv_count, sl.q_count
         lens = seq_lens(cfg, args.seed, 0)
+        global_b = len(lens)
     else:
-        lens = seq_lens(cfg, args.seed, rank)
+        lens, global_b = rank_lens(cfg, args, world, rank)
     kcfg = dict(cfg, Hkv=Hkv, Hq=Hq)
     B = len(lens)
     steps = args.warmup + args.steps
@@ -425,7 +457,7 @@ def run_ours(cfg, args, world, rank, local):
                dec_launches=L * args.steps, launches=launches, clocks=clocks,
                e2e_ms=e2e_ms, e2e_kv=e2e_kv,
                h2d=(hk[0].numel() + hv[0].numel() + hq[0].numel()) * 2,
-               d2h=ho[0].numel() * 2, B=B, lens=lens)
+               d2h=ho[0].numel() * 2, B=B, global_b=global_b, lens=lens)
     cache.close()
     return res
 
@@ -903,7 +935,7 @@ def run_reference(cfg, args, world, rank, local):
     if lib is None:
         return None, why
     L, Hq, Hkv, D = cfg["L"], cfg["Hq"], cfg["Hkv"], cfg["D"]
-    lens = seq_lens(cfg, args.seed, rank)
+    lens, global_b = rank_lens(cfg, args, world, rank)
     if len(set(lens)) != 1:
         return None, "reference arm runs uniform-length configs only (one attention_decode per layer)"
     B, P = len(lens), lens[0]
@@ -1007,7 +1039,8 @@ def run_reference(cfg, args, world, rank, local):
     e2e_ms = e_start.elapsed_time(e_end)
     lib.ref_kv_destroy(h)
     return dict(ms=ms, kv=kv_total, dec_ms=dec_ms, clocks=clocks, e2e_ms=e2e_ms, e2e_kv=e2e_kv,
-                h2d=(hk.numel() + hv.numel() + hq.numel()) * 2, d2h=ho.numel() * 2, B=B), None
+                h2d=(hk.numel() + hv.numel() + hq.numel()) * 2, d2h=ho.numel() * 2, B=B,
+                global_b=global_b), None
 
 
 # ------------------------------------------------------------ CPU baseline --
@@ -1061,8 +1094,11 @@ def main():
                          "publishes a flag, then pulls the other ranks' slices over NVLink), "
                          "or an NCCL all-gather after each layer")
     ap.add_argument("--shard", choices=["batch", "head"], default="batch",
-                    help="multi-GPU split: whole sequences per rank (weak scaling) or KV heads "
-                         "per rank with an all-gather of outputs each layer (strong scaling)")
+                    help="multi-GPU split: whole sequences per rank, or KV heads per rank with "
+                         "an all-gather of outputs each layer")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="batch shard: strong splits the config's batch over the ranks (fixed "
+                         "total work); weak gives every rank the whole batch")
     ap.add_argument("--flow", choices=["fused", "layer"], default="fused",
                     help="fused: one append of every layer's new token, then decode per layer; "
                          "layer: per layer, append that layer's token then decode with RoPE on Q "
@@ -1092,7 +1128,10 @@ def main():
                                    + ("a flag publish and NVLink pull fused into the decode call)"
                                       if args.gather == "p2p" else "NCCL all-gather)")
                                    if args.shard == "head" else
-                                   f"batch-shard x{world} (independent sequences per GPU)"),
+                                   f"batch-shard x{world} (" + ("the batch split over the GPUs by KV bytes"
+                                                               if args.scaling == "strong" else
+                                                               "a whole batch per GPU") +
+                                   ", independent sequences, no collective)"),
                    "l2": "KV bytes per step far above the 126 MB L2; no flush needed",
                    "flow": ("per layer: append that layer's token, decode with RoPE on Q "
                             "(tl_attention_step)" if args.flow == "layer" else
@@ -1152,6 +1191,7 @@ def main():
                 dist.destroy_process_group()
             return
         ms = barrier_max(res["ms"], world)
+        rank_ms = gather_values(res["ms"], world)
         kv = barrier_sum(res["kv"], world)
         e2e_ms = barrier_max(res["e2e_ms"], world)
         e2e_kv = barrier_sum(res["e2e_kv"], world)
@@ -1163,9 +1203,11 @@ def main():
                     "steps": args.steps, "warmup": args.warmup,
                     "ms_per_step": round(ms / args.steps, 4),
                     "us_per_step": round(1e3 * ms / args.steps, 1),
-                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "per_rank_ms_per_step": [round(x / args.steps, 4) for x in rank_ms],
+                    "higher_is_better": True, "scaling": args.scaling if world > 1 else "strong",
+                    "vs_baseline": None,
                     "dtype": "f16 (fp32 accumulate)", "data": "synthetic N(0,1) fp16, seeded",
-                    "config": dict(base_config, global_batch=res["B"] * world, layout="reference contiguous slots + [B][H][S][D] kernel input"),
+                    "config": dict(base_config, global_batch=res["global_b"], layout="reference contiguous slots + [B][H][S][D] kernel input"),
                     "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": 0,
                                      "kind": "reference",
                                      "sample": "the reference's own CUDA path (appendKV memcpys + attention_decode) rebuilt for sm_100a, on the GPU: the reference has no host implementation of this path"},
@@ -1307,6 +1349,7 @@ def main():
 
     res = run_ours(cfg, args, world, rank, local)
     ms = barrier_max(res["ms"], world)
+    rank_ms = gather_values(res["ms"], world)
     kv = barrier_sum(res["kv"], world)
     e2e_ms = barrier_max(res["e2e_ms"], world)
     e2e_kv = barrier_sum(res["e2e_kv"], world)
@@ -1326,10 +1369,12 @@ def main():
                 "ms_per_step": round(ms / args.steps, 4),
                 "us_per_step": round(1e3 * ms / args.steps, 1),
                 "pct_hbm_peak_per_gpu": round(100 * value / world / peak, 1),
-                "higher_is_better": True, "scaling": "strong" if args.shard == "head" else "weak",
+                "per_rank_ms_per_step": [round(x / args.steps, 4) for x in rank_ms],
+                "higher_is_better": True,
+                "scaling": "strong" if args.shard == "head" or world == 1 else args.scaling,
                 "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
                 "data": "synthetic N(0,1) fp16 K/V/Q from a seeded generator (no dataset)",
-                "config": dict(base_config, global_batch=res["B"] * (1 if args.shard == "head" else world),
+                "config": dict(base_config, global_batch=res["global_b"],
                                seq_len=max(res["lens"])),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                              "unit": "GB/s", "frac": round(achieved / peak, 4),

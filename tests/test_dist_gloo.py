@@ -158,3 +158,27 @@ def test_rank_that_exits_between_steps_makes_the_next_collective_raise():
     res = _run(2, "dies")
     assert res[1] == "exited"
     assert res[0].startswith("error:"), res[0]
+
+
+def test_bench_strong_scaling_splits_the_config_batch():
+    """bench.py --gpus N (strong scaling, the default): the ranks' sequences
+    together are the config's batch, each exactly once, balanced by KV bytes
+    to within one sequence; --scaling weak gives every rank a whole batch."""
+    import argparse
+    import importlib
+    import sys as _sys
+
+    _sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    bench = importlib.import_module("bench")
+    for name in ("c2", "c3", "c4", "c5s"):
+        cfg = bench.CONFIGS[name]
+        full = bench.seq_lens(cfg, 0, 0)
+        for world in (1, 2, 4, 8):
+            args = argparse.Namespace(seed=0, scaling="strong")
+            parts = [bench.rank_lens(cfg, args, world, r) for r in range(world)]
+            assert all(gb == len(full) for _, gb in parts)
+            assert sorted(x for lens, _ in parts for x in lens) == sorted(full)
+            loads = [sum(lens) for lens, _ in parts]
+            assert max(loads) - min(loads) <= max(full), (name, world, loads)
+        weak = [bench.rank_lens(cfg, argparse.Namespace(seed=0, scaling="weak"), 4, r) for r in range(4)]
+        assert all(len(lens) == len(full) and gb == 4 * len(full) for lens, gb in weak)
