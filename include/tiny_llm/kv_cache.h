@@ -1,12 +1,25 @@
 // tiny_llm::KVCacheManager over the B200 paged KV cache (C-ABI tllm_kv.h).
 //
-// Keeps every signature of the reference class (include/tiny_llm/kv_cache.h:
-// 24-111 in AICL-Lab/tiny-llm): create / allocateSequence / releaseSequence /
-// getCache / getCacheChecked / appendKV / advanceSeqLen / getSeqLen /
-// hasSequence / memory statistics / getActiveSequenceCount / getConfig, the
-// non-copyable, non-movable ownership and the error texts. It adds the paged
-// and fused entry points (reserve, appendKVAllLayers, decodeAttention,
-// getBlockTable, getPoolStats).
+// Drop-in for the reference header include/tiny_llm/kv_cache.h (AICL-Lab/
+// tiny-llm, :24-111): every signature of the reference class (create /
+// allocateSequence / releaseSequence / getCache / getCacheChecked / appendKV /
+// advanceSeqLen / getSeqLen / hasSequence / memory statistics /
+// getActiveSequenceCount / getConfig), its non-copyable, non-movable
+// ownership and its error texts; plus the paged and fused entry points
+// (reserve, appendKVAllLayers, decodeAttention, attentionStep,
+// prefillAttention, projectQKVAppend, getBlockTable, getPoolStats).
+//
+// Two ways to build it:
+//  - inside the tiny-llm tree (this directory ahead of the engine's include
+//    directory, or this file in place of the engine's kv_cache.h): the
+//    engine's tiny_llm/types.h supplies KVCacheConfig (types.h:122-128) and
+//    its tiny_llm/result.h supplies Result<T>, so the engine's own sources
+//    compile against this header unchanged;
+//  - standalone (no tiny_llm/types.h on the include path, or
+//    TLLM_KV_STANDALONE defined): tllm_result.h supplies Result<T> and the
+//    five-field KVCacheConfig is declared here with the reference's defaults.
+// Either way PagedKVCacheConfig extends KVCacheConfig with the pool and RoPE
+// settings; create(const KVCacheConfig &) takes the paged defaults.
 //
 // Behavioural differences, by design:
 //  - memory is a pool of fixed-size blocks; a sequence takes one block at
@@ -14,6 +27,9 @@
 //  - getCache() points at the sequence's first block of the layer, which
 //    (token-major layout) holds tokens 0..block_size-1 as [pos][Hkv][D];
 //  - CUDA failures are returned as errors instead of thrown.
+// The class is defined in tiny-llm_b200/csrc/kv_cache_manager.cpp, which the
+// user compiles with the same include paths (the result and config types
+// above belong to the user's build); it calls libtllm_kv.so's C-ABI.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -24,20 +40,34 @@
 #include <utility>
 #include <vector>
 
-#include "tiny_llm/result.h"
+#if !defined(TLLM_KV_STANDALONE) && __has_include("tiny_llm/types.h")
+#include "tiny_llm/types.h"  // the engine's KVCacheConfig and Result<T>
+#if __has_include("tiny_llm/cuda_utils.h")
+#include "tiny_llm/cuda_utils.h"  // included by the header this one replaces
+#endif
+#define TLLM_KV_ENGINE_TYPES 1
+#else
+#include "tllm_result.h"
+#endif
 #include "tllm_kv.h"
 
 namespace tiny_llm {
 
-// Reference KVCacheConfig (include/tiny_llm/types.h:122-128) plus the paged
-// pool and RoPE settings. num_heads is the KV-head count, as the reference
-// engine passes it (src/inference_engine.cpp:59).
+#ifndef TLLM_KV_ENGINE_TYPES
+// Reference KVCacheConfig (include/tiny_llm/types.h:122-128). num_heads is
+// the KV-head count, as the reference engine passes it
+// (src/inference_engine.cpp:59).
 struct KVCacheConfig {
     int num_layers = 32;
     int num_heads = 32;
     int head_dim = 128;
     int max_seq_len = 2048;
     int max_batch_size = 1;
+};
+#endif
+
+// KVCacheConfig plus the paged pool, query heads and RoPE settings.
+struct PagedKVCacheConfig : KVCacheConfig {
     int block_size = 16;
     long long num_blocks = 0;  // 0: max_batch_size * ceil(max_seq_len / block_size)
     int num_q_heads = 0;       // 0: num_heads (MHA)
@@ -46,11 +76,17 @@ struct KVCacheConfig {
     int layout = TL_LAYOUT_TOKEN_MAJOR;
     int backend = TL_BACKEND_CUDA;
     int device = -1;
+
+    PagedKVCacheConfig() = default;
+    explicit PagedKVCacheConfig(const KVCacheConfig &base) : KVCacheConfig(base) {}
 };
 
 class KVCacheManager {
   public:
+    // The reference factory: a paged pool with the default block size, MHA
+    // (query heads = config.num_heads) and no RoPE.
     static Result<std::unique_ptr<KVCacheManager>> create(const KVCacheConfig &config);
+    static Result<std::unique_ptr<KVCacheManager>> create(const PagedKVCacheConfig &config);
     ~KVCacheManager();
 
     KVCacheManager(const KVCacheManager &) = delete;
@@ -72,6 +108,7 @@ class KVCacheManager {
     size_t getFreeMemory() const noexcept;
     int getActiveSequenceCount() const noexcept;
     const KVCacheConfig &getConfig() const noexcept { return config_; }
+    const PagedKVCacheConfig &getPagedConfig() const noexcept { return config_; }
 
     // Paged / fused additions.
     Result<void> reserve(int seq_id, int new_len);
@@ -106,10 +143,10 @@ class KVCacheManager {
     tl_cache *handle() noexcept { return h_; }
 
   private:
-    explicit KVCacheManager(const KVCacheConfig &config) : config_(config) {}
+    explicit KVCacheManager(const PagedKVCacheConfig &config) : config_(config) {}
     Result<void> status(int code) const;
 
-    KVCacheConfig config_;
+    PagedKVCacheConfig config_;
     tl_cache *h_ = nullptr;
 };
 

@@ -1,9 +1,13 @@
-// Result<T>: value-or-message return type of the tiny_llm C++ API.
+// tiny_llm::Result<T> for builds of this library's C++ facade that do not
+// have tiny-llm's own headers (the facade's tests, standalone users).
 //
-// Interface kept alike with the reference's include/tiny_llm/result.h:11-112
-// (ok/err factories, isOk/isErr, value() that throws on error, error() that
-// throws on ok, valueOr, and a Result<void> specialisation) so code written
-// against tiny-llm's KVCacheManager compiles unchanged.
+// Inside the tiny-llm engine tree, include/tiny_llm/kv_cache.h uses the
+// engine's own tiny_llm/result.h instead and this file is never included, so
+// the two definitions never meet. The interface is kept alike with the
+// reference's include/tiny_llm/result.h:11-112 (ok/err factories,
+// isOk/isErr, value() that throws on error, error() that throws on ok,
+// valueOr, map, flatMap with ValueType, and a Result<void> specialisation) so
+// code written against tiny-llm's KVCacheManager compiles with either.
 #pragma once
 
 #include <stdexcept>
@@ -37,6 +41,22 @@ class Result {
         return std::get<1>(state_);
     }
     T valueOr(T fallback) const { return isOk() ? std::get<0>(state_) : std::move(fallback); }
+
+    // f(T) -> U; an error passes through with its message.
+    template <typename F>
+    auto map(F &&f) -> Result<decltype(f(std::declval<T>()))> {
+        using U = decltype(f(std::declval<T>()));
+        if (isErr()) return Result<U>::err(error());
+        return Result<U>::ok(f(value()));
+    }
+
+    // f(T) -> Result<U>; an error passes through with its message.
+    template <typename F>
+    auto flatMap(F &&f) -> decltype(f(std::declval<T>())) {
+        using R = decltype(f(std::declval<T>()));
+        if (isErr()) return R::err(error());
+        return f(value());
+    }
 
   private:
     template <std::size_t I, typename U>

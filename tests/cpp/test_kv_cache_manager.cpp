@@ -29,9 +29,9 @@ static int g_failed = 0, g_passed = 0;
         }                                                                              \
     } while (0)
 
-static KVCacheConfig createConfig(int num_layers = 2, int num_heads = 4, int head_dim = 64,
+static PagedKVCacheConfig createConfig(int num_layers = 2, int num_heads = 4, int head_dim = 64,
                                   int max_seq_len = 128, int max_batch_size = 4) {
-    KVCacheConfig c;
+    PagedKVCacheConfig c;
     c.num_layers = num_layers;
     c.num_heads = num_heads;
     c.head_dim = head_dim;
@@ -41,7 +41,7 @@ static KVCacheConfig createConfig(int num_layers = 2, int num_heads = 4, int hea
     return c;
 }
 
-static std::unique_ptr<KVCacheManager> createCache(const KVCacheConfig &c) {
+static std::unique_ptr<KVCacheManager> createCache(const PagedKVCacheConfig &c) {
     auto r = KVCacheManager::create(c);
     if (r.isErr()) std::fprintf(stderr, "  create failed: %s\n", r.error().c_str());
     EXPECT(r.isOk());
@@ -212,6 +212,39 @@ int main(int argc, char **argv) {
         EXPECT(has(call(0, H(256), 256, H(256), 32, {id, id}), "duplicate"));
         if (!g_gpu) EXPECT(has(call(0, H(256), 256, H(256), 32, {id}), "no CUDA device"));
         EXPECT(cache->getSeqLen(id) == 0);
+    });
+    run("ResultMapAndFlatMap", [] {  // the reference's tests/test_cuda_utils.cpp:46,53 use them
+        auto doubled = Result<int>::ok(21).map([](int x) { return 2 * x; });
+        EXPECT(doubled.isOk() && doubled.value() == 42);
+        auto failed = Result<int>::err("boom").map([](int x) { return x + 1; });
+        EXPECT(failed.isErr() && failed.error() == "boom");
+        auto chained = Result<int>::ok(5).flatMap([](int x) {
+            return x > 3 ? Result<std::string>::ok(std::to_string(x)) : Result<std::string>::err("small");
+        });
+        EXPECT(chained.isOk() && chained.value() == "5");
+        auto stopped = Result<int>::ok(1).flatMap([](int x) {
+            return x > 3 ? Result<std::string>::ok("big") : Result<std::string>::err("small");
+        });
+        EXPECT(stopped.isErr() && stopped.error() == "small");
+    });
+    run("ReferenceConfigCreatesMhaPagedCache", [] {  // create(const KVCacheConfig &)
+        KVCacheConfig base;
+        base.num_layers = 2;
+        base.num_heads = 4;
+        base.head_dim = 64;
+        base.max_seq_len = 100;
+        base.max_batch_size = 3;
+        PagedKVCacheConfig paged(base);
+        paged.backend = g_gpu ? TL_BACKEND_CUDA : TL_BACKEND_HOST_BOOKKEEPING;
+        auto cache = createCache(paged);
+        EXPECT(cache->getConfig().num_heads == 4 && cache->getConfig().max_batch_size == 3);
+        EXPECT(cache->getPagedConfig().block_size == 16 && !cache->getPagedConfig().rope_on_append);
+        EXPECT(cache->getTotalMemory() > 0);
+        if (g_gpu) {  // the five-field reference config alone: CUDA backend defaults
+            auto r = KVCacheManager::create(base);
+            EXPECT(r.isOk());
+            EXPECT(r.value()->getPagedConfig().num_q_heads == 0);
+        }
     });
     if (g_gpu) {
         run("KVCacheAppendRetrieve", [] {  // tests/test_transformer.cu:141-194

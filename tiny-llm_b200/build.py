@@ -31,7 +31,10 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-r
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter"]
 
 CU_SOURCES = ["kv_append.cu", "paged_decode.cu", "paged_prefill_tc.cu", "qkv_append.cu", "sampling.cu", "decode_static_scratch.cu"]
-CPP_SOURCES = ["paged_kv.cpp", "kv_cache_manager.cpp"]
+CPP_SOURCES = ["paged_kv.cpp"]
+# The C++ facade (tiny_llm::KVCacheManager) is compiled by its user, with the
+# user's include paths; the library itself exports only the C-ABI.
+FACADE_SOURCE = CSRC / "kv_cache_manager.cpp"
 HEADERS = ["kernels.h", "paged_kv.h", "ptx.cuh"]
 
 
@@ -53,8 +56,7 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     """Compiles and links libtllm_kv.so; returns its path."""
     BUILD.mkdir(exist_ok=True)
     LIB_DIR.mkdir(exist_ok=True)
-    common = [CSRC / h for h in HEADERS] + [INCLUDE / "tllm_kv.h", INCLUDE / "tiny_llm" / "kv_cache.h",
-                                            INCLUDE / "tiny_llm" / "result.h", Path(__file__)]
+    common = [CSRC / h for h in HEADERS] + [INCLUDE / "tllm_kv.h", Path(__file__)]
     inc = [f"-I{INCLUDE}", f"-I{CSRC}", f"-I{CUDA_HOME / 'include'}"]
     objs = []
     for src in CU_SOURCES:
@@ -88,8 +90,10 @@ def build_cpp_tests(force: bool = False) -> Path:
     lib = build_library()
     src = ROOT / "tests" / "cpp" / "test_kv_cache_manager.cpp"
     out = BUILD / "test_kv_cache_manager"
-    if force or _stale(out, [src, lib, INCLUDE / "tiny_llm" / "kv_cache.h"]):
-        cmd = [CXX, "-O1", "-std=c++17", f"-I{INCLUDE}", f"-I{CUDA_HOME / 'include'}", str(src),
+    if force or _stale(out, [src, lib, FACADE_SOURCE, INCLUDE / "tiny_llm" / "kv_cache.h",
+                             INCLUDE / "tllm_result.h"]):
+        cmd = [CXX, "-O1", "-std=c++17", "-Wall", "-Wextra", "-Wno-unused-parameter", f"-I{INCLUDE}",
+               f"-I{CUDA_HOME / 'include'}", str(src), str(FACADE_SOURCE),
                "-o", str(out), f"-L{LIB_DIR}", "-ltllm_kv", f"-Wl,-rpath,{LIB_DIR}",
                f"-L{CUDA_HOME / 'lib64'}", "-lcudart", f"-Wl,-rpath,{CUDA_HOME / 'lib64'}"]
         _run(cmd)

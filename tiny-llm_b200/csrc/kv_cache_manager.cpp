@@ -1,10 +1,18 @@
 // tiny_llm::KVCacheManager: the reference's C++ API
 // (include/tiny_llm/kv_cache.h:24-111) as a thin layer over the C-ABI.
+// Compiled by the user of the facade with the user's include paths, so that
+// Result<T> and KVCacheConfig are the ones the rest of that build sees (the
+// tiny-llm engine's own, or tllm_result.h's standalone); libtllm_kv.so
+// carries only the C-ABI.
 #include "tiny_llm/kv_cache.h"
 
 namespace tiny_llm {
 
 Result<std::unique_ptr<KVCacheManager>> KVCacheManager::create(const KVCacheConfig &config) {
+    return create(PagedKVCacheConfig(config));
+}
+
+Result<std::unique_ptr<KVCacheManager>> KVCacheManager::create(const PagedKVCacheConfig &config) {
     tl_config c;
     tl_config_init(&c);
     c.num_layers = config.num_layers;
