@@ -280,6 +280,7 @@ def _close_f16_rows(got, exp, what):
     (128, 1, 16, True, T.TL_LAYOUT_HEAD_MAJOR, 33, 1024, 128),
     (64, 8, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 64, 384, 64),
     (128, 4, 16, False, T.TL_LAYOUT_TOKEN_MAJOR, 70, 256, 32),
+    (128, 4, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 33, 512, 16),
 ])
 def test_project_qkv_append(D, G, bs, rope, layout, B, hidden, group):
     """Fused W8A16 Q/K/V projection of one decode token per sequence
@@ -287,7 +288,8 @@ def test_project_qkv_append(D, G, bs, rope, layout, B, hidden, group):
     Q and the K/V rows written at each sequence's length match the oracle's
     restatement of the reference matmul rounded to fp16 (then rotated at
     that position when the cache rotates on append); every earlier row of
-    the pool is untouched. B = 70 runs as two launches."""
+    the pool is untouched. B = 70 runs as two launches. Group 16 runs the
+    mma.sync kernel, the other groups the tcgen05 kernel."""
     import torch
     Hkv = 2
     Hq = Hkv * G

@@ -86,3 +86,6 @@ def test_sample_tokens_validates_arguments():
         T.sample_tokens(16, 4, 2, 8, 16)
     assert "row_stride" in str(e.value)
     T.sample_tokens(16, 8, 0, 8, 16)  # no rows: nothing to do
+    with pytest.raises(T.Unsupported) as e:  # one row's slices must fit the cluster's shared memory
+        T.sample_tokens(16, 600000, 1, 600000, 16)
+    assert "vocab above" in str(e.value)

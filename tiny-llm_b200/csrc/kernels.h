@@ -155,6 +155,11 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s);
 cudaError_t launch_apply_deltas(const DeltaArgs &a, cudaStream_t s);
 // Encodes the tensor map once per pool (stored opaque, 128 bytes).
 cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128);
+// A 2-D tensor map (128-byte swizzle, zero fill out of bounds) over a
+// row-major [outer][inner] array of uint8 or fp16 with rows row_bytes apart.
+cudaError_t encode_tensor_map_2d(void *tmap_out128, bool fp16, const void *base, unsigned long long inner,
+                                 unsigned long long outer, unsigned long long row_bytes, unsigned box_inner,
+                                 unsigned box_outer);
 cudaError_t launch_decode(const DecodeArgs &a, const void *tmap128, cudaStream_t s);
 cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s);
 // One fused Q/K/V projection + append launch (decode: one token per row).
@@ -179,7 +184,7 @@ struct QkvArgs {
     int row_pos[kMaxQkvRows];
 };
 
-// Token sampling, one CTA per row of logits.
+// Token sampling, one cluster of CTAs per row of logits.
 struct SampleArgs {
     const void *logits;       // fp16 [rows] rows of `vocab`, row_stride elements apart
     long long row_stride;
@@ -192,12 +197,24 @@ struct SampleArgs {
     int *tokens;              // device [rows]
 };
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s);
+int sample_max_vocab();  // largest vocabulary a row may have
 
 int prefill_tc_rows_per_cta();
 cudaError_t launch_prefill_tc(const PrefillArgs &a, const void *tmap128, cudaStream_t s);
 int qkv_k_block();
 int qkv_rows_padded(int rows);  // the kernel's row tile for a launch of `rows` rows
 cudaError_t launch_qkv_append(const QkvArgs &a, cudaStream_t s);
+// The tcgen05 variant (qkv_append_tc.cu): weight columns in tiles of 128
+// (Q, K and V each a multiple of 128 columns), group 32/64/128, weights
+// 16-byte aligned, ksplit <= 16. partial: fp32 [ksplit][columns / 128]
+// [qkv_tc_rows_padded][128] (every launch overwrites what it reads);
+// counters: [columns / 128], zero between launches. qkv_tc_split picks the
+// split of K for a launch of `rows` rows; false when no split keeps the
+// group accumulators within TMEM (the mma.sync kernel runs instead).
+bool qkv_tc_supported(int head_dim, int group, int nq, int nkv, int hidden);
+int qkv_tc_rows_padded(int rows);
+bool qkv_tc_split(int hidden, int group, int rows, int tiles, int num_sms, int *ksplit, int *kchunk);
+cudaError_t launch_qkv_append_tc(const QkvArgs &a, cudaStream_t s);
 
 
 }  // namespace tllm

@@ -931,9 +931,9 @@ cudaError_t launch_merge(const DecodeArgs &a, cudaStream_t s) {
     }
 }
 
-cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128) {
-    // resolved once, by a thread-safe static initialiser (first calls may
-    // come from several host threads at once)
+// The driver's tensor-map encoder, resolved once by a thread-safe static
+// initialiser (first calls may come from several host threads at once).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static const PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
         cudaDriverEntryPointQueryResult q;
         void *fn = nullptr;
@@ -942,6 +942,27 @@ cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128) {
         if (e != cudaSuccess || q != cudaDriverEntryPointSuccess) fn = nullptr;
         return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }();
+    return encode;
+}
+
+cudaError_t encode_tensor_map_2d(void *tmap_out128, bool fp16, const void *base, unsigned long long inner,
+                                 unsigned long long outer, unsigned long long row_bytes, unsigned box_inner,
+                                 unsigned box_outer) {
+    const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return cudaErrorNotSupported;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer}, estr[2] = {1, 1};
+    CUresult r = encode(static_cast<CUtensorMap *>(tmap_out128),
+                        fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                        const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t encode_pool_tensor_map(const PoolGeom &g, void *tmap_out128) {
+    const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (!encode) return cudaErrorNotSupported;
     const unsigned long long L2 = 2ull * g.num_layers;
     cuuint64_t dims[3], strides[2];

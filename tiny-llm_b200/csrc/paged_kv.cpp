@@ -1103,17 +1103,40 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
     DeviceGuard guard(c);
     const int Hkv = c->cfg.num_kv_heads, Hq = Hkv * c->group;
     const int tiles = Hq + 2 * Hkv;
-    // split-K: about three CTAs per SM (2 and 4 measured slower); a chunk's
-    // activations stay under ~100 KB of shared memory
-    const int kblk = tllm::qkv_k_block(), nkb = hidden / kblk;
     const int rows_max = std::min(num_seqs, tllm::kMaxQkvRows);
-    const int rpad = tllm::qkv_rows_padded(rows_max);  // the largest launch's row tile
-    const int kb_cap = std::max(1, (100 * 1024 / (2 * rpad) - 8) / kblk);
-    int ks = std::max(1, (3 * std::max(c->num_sms, 1) + tiles / 2) / tiles);
-    ks = std::min(ks, nkb);
-    int kbc = std::min((nkb + ks - 1) / ks, kb_cap);
-    ks = (nkb + kbc - 1) / kbc;
-    const size_t need = ks > 1 ? (size_t)tiles * rpad * D : 0;  // one fp32 accumulator per column tile
+    // tcgen05 kernel where the columns come in tiles of 128 and the weights
+    // allow 16-byte loads; the mma.sync kernel otherwise
+    // (and a split of K whose group accumulators fit TMEM, for every
+    // launch: a full one of rows_max rows and the last, shorter one)
+    const int tiles128 = (Hq + 2 * Hkv) * D / 128;
+    const int rows_last = num_seqs % tllm::kMaxQkvRows;
+    auto tc_plan = [&](int n, int *ks_, int *kchunk_) {
+        return tllm::qkv_tc_split(hidden, group_size, n, tiles128, c->num_sms, ks_, kchunk_);
+    };
+    int ks, kchunk;
+    bool tc = tllm::qkv_tc_supported(D, group_size, Hq * D, Hkv * D, hidden) && !mis(wq, 16) &&
+              !mis(wk, 16) && !mis(wv, 16) && tc_plan(rows_max, &ks, &kchunk);
+    int ks_last = 0, kchunk_last = 0;
+    if (tc && rows_last > 0 && num_seqs > tllm::kMaxQkvRows) tc = tc_plan(rows_last, &ks_last, &kchunk_last);
+    size_t need;
+    if (tc) {
+        // one fp32 slot per split and column tile
+        need = ks > 1 ? (size_t)ks * tiles128 * tllm::qkv_tc_rows_padded(rows_max) * 128 : 0;
+        if (ks_last > 1)
+            need = std::max(need, (size_t)ks_last * tiles128 * tllm::qkv_tc_rows_padded(rows_last) * 128);
+    } else {
+        // split-K: about three CTAs per SM (2 and 4 measured slower); a chunk's
+        // activations stay under ~100 KB of shared memory
+        const int kblk = tllm::qkv_k_block(), nkb = hidden / kblk;
+        const int rpad = tllm::qkv_rows_padded(rows_max);  // the largest launch's row tile
+        const int kb_cap = std::max(1, (100 * 1024 / (2 * rpad) - 8) / kblk);
+        ks = std::max(1, (3 * std::max(c->num_sms, 1) + tiles / 2) / tiles);
+        ks = std::min(ks, nkb);
+        const int kbc = std::min((nkb + ks - 1) / ks, kb_cap);
+        ks = (nkb + kbc - 1) / kbc;
+        kchunk = kbc * kblk;
+        need = ks > 1 ? (size_t)tiles * rpad * D : 0;  // one fp32 accumulator per column tile
+    }
     std::string why;
     if (need > c->qkv_partial_floats) {
         storage_free(c, c->qkv_partial);
@@ -1171,7 +1194,11 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
         a.rows = n;
         a.num_q_heads = Hq;
         a.ksplit = ks;
-        a.kchunk = kbc * kblk;
+        a.kchunk = kchunk;
+        if (tc && n != rows_max) {  // the last, shorter launch has its own split
+            a.ksplit = ks_last;
+            a.kchunk = kchunk_last;
+        }
         a.q_out = static_cast<uint16_t *>(q_out) + r0 * nq;
         if (c->cfg.rope_on_append) {
             a.rope_cos = c->rope_cos;
@@ -1185,7 +1212,8 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
             a.row_block[j] = rb[(size_t)(r0 + j)];
             a.row_pos[j] = rp[(size_t)(r0 + j)];
         }
-        cudaError_t e = tllm::launch_qkv_append(a, (cudaStream_t)stream);
+        cudaError_t e = tc ? tllm::launch_qkv_append_tc(a, (cudaStream_t)stream)
+                           : tllm::launch_qkv_append(a, (cudaStream_t)stream);
         if (e != cudaSuccess) return cuda_fail(c, e, "projectQKVAppend: launch failed");
         ++c->launches;
     }
@@ -1204,6 +1232,9 @@ int tl_sample_tokens(const void *logits, long long row_stride, int rows, int voc
         return st;
     };
     if (rows < 0 || vocab <= 0) return fail(TL_ERR_INVALID_ARG, "sampleTokens: rows must be >= 0 and vocab > 0");
+    if (vocab > tllm::sample_max_vocab() || rows > (1 << 27))
+        return fail(TL_ERR_UNSUPPORTED, "sampleTokens: vocab above " + std::to_string(tllm::sample_max_vocab()) +
+                                            " or more than 2^27 rows is not supported");
     if (rows == 0) return TL_OK;
     if (!logits || !tokens_out)
         return fail(TL_ERR_INVALID_ARG, !logits ? "sampleTokens: logits is null" : "sampleTokens: tokens is null");

@@ -179,6 +179,52 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void *tmap, uint
         : "memory");
 }
 
+// 2-D tiled TMA load global -> shared, completing on an mbarrier. No
+// multicast: the source is always this GPU's own memory.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint32_t bar, int x, int y,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+// 2-D tiled TMA prefetch global -> L2 (no shared memory, no barrier). L2 is
+// the device's point of coherence, so a later load still sees any write
+// made after the prefetch.
+__device__ __forceinline__ void tma_prefetch_2d(const void *tmap, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
+// A 16x16 tile of bytes (rows at the addresses of threads 0-15), transposed:
+// thread (g = lane / 4, t = lane % 4) receives r0 = bytes (4t..4t+3, g) and
+// r1 = bytes (4t..4t+3, g + 8) as (row, column) of the stored tile, the
+// lowest row in the lowest byte.
+__device__ __forceinline__ void ldmatrix_m16n16_trans_b8(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+    asm volatile("ldmatrix.sync.aligned.m16n16.x1.trans.shared.b8 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// 16 TMEM lanes x 8 columns from a warp: thread (g = lane / 4, t = lane % 4)
+// writes r0, r1 to lane g, columns 2t, 2t + 1 and r2, r3 to lane g + 8,
+// the same columns (relative to taddr).
+__device__ __forceinline__ void tmem_st_16x256b(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x1.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
+}
+
+// Device-scope fetch-and-add with acquire-release semantics (the arrival of
+// a split-K CTA: its partial sums before, the last arrival's reads after).
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // L2 policy for streamed-once data (KV tiles are read once per decode).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;

@@ -17,21 +17,41 @@
 // std::discrete_distribution, so tokens match in distribution, not draw by
 // draw.
 //
-// One CTA per row. fp16 logits map to 16-bit keys that order like the
-// values (-0 folded into +0, NaN lowest), so thresholds and the draw are
-// found with 256-bin histograms over the key's high byte, then its low byte
-// within one bin (counts for top-k, probability mass for top-p and the
-// draw), and the index among equal keys with one block-wide scan. Every pass
-// reads the row again (from L2 after the first).
+// One thread-block cluster of kCtas CTAs per row. Each CTA owns a contiguous
+// slice of the row, reads it from global memory once and keeps it in shared
+// memory as 16-bit keys that order like the values (-0 folded into +0, NaN
+// lowest and weightless). Thresholds and the draw are found with 256-bin
+// histograms over the key's high byte, then its low byte within one bin
+// (counts for top-k, probability mass for top-p and the draw). Masses are
+// exact integers: each weight exp((l - max) / T) <= 1 in units of 2^-40, so
+// histogram sums are associative and every CTA of the cluster derives the
+// same thresholds. Every warp fills its own histogram copy (no atomics
+// between warps), the CTA sums its copies, every CTA sums the cluster's CTA
+// histograms through distributed shared memory, and one warp turns the
+// result into suffix sums and finds thresholds with ballots. The index
+// among equal keys comes from per-CTA counts, a prefix over the cluster's
+// ranks (slices are in index order) and one block-wide scan in the CTA that
+// holds it.
+#include <cooperative_groups.h>
 #include <cstdint>
 #include <cuda_fp16.h>
+#include <map>
+#include <mutex>
 
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace tllm {
 namespace {
 
-constexpr int kSampleThreads = 1024;
+constexpr int kCtas = 8;          // CTAs per row (one cluster)
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxSlice = 65536;  // keys per CTA: vocabularies up to kCtas * kMaxSlice
+constexpr float kFx = 1099511627776.0f;  // 2^40: the unit of an integer mass
+
+using u64 = unsigned long long;
 
 __device__ __forceinline__ uint32_t key_of(uint16_t h) {
     if ((h & 0x7C00u) == 0x7C00u && (h & 0x03FFu) != 0) return 0u;  // NaN: below everything
@@ -54,296 +74,405 @@ __device__ __forceinline__ float uniform_of(unsigned long long seed, unsigned lo
     return (float)(z >> 40) * (1.0f / 16777216.0f);
 }
 
-template <typename T, typename Op>
-__device__ T block_reduce(T v, Op op, T *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// What every CTA publishes for the others to read. Double-buffered: a buffer
+// is written again two reductions later, after the cluster barrier that
+// follows every reader's use of it.
+struct Pub {
+    u64 mass[256];
+    unsigned cnt[256];
+    u64 best;
+    unsigned count;
+};
+
+struct Shared {
+    u64 wmass[kWarps][256];  // per-warp histograms
+    unsigned wcnt[kWarps][256];
+    u64 gmass[256];          // the cluster's histograms of the last pass
+    unsigned gcnt[256];
+    u64 amass[256];          // their suffix sums: bins above b
+    unsigned acnt[256];
+    u64 hmass1[256];         // the first pass's masses and suffix sums
+    u64 amass1[256];
+    Pub pub[2];
+    u64 red64[kWarps];
+    unsigned redu[kWarps];
+    unsigned wpre[kWarps];
+    u64 s_u[4];
+    int s_int[4];
+};
+
+__device__ __forceinline__ u64 warp_max64(u64 v) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        v = red[lane];  // blockDim.x == 1024: 32 warps
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) red[0] = v;
+    for (int o = 16; o > 0; o >>= 1) {
+        const u64 t = __shfl_xor_sync(0xffffffffu, v, o);
+        v = t > v ? t : v;
     }
-    __syncthreads();
-    const T r = red[0];
-    __syncthreads();
-    return r;
+    return v;
+}
+__device__ __forceinline__ int warp_max_int(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_min_int(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ unsigned warp_sum(unsigned v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
 }
 
-// Scans a 256-bin histogram from the top bin down; returns the bin where the
-// running total first exceeds `target` (or reaches it, when `reach`), and
-// the total of the bins above it. -1 when it never does.
+// One warp: above[b] = sum of h over the bins above b (lane l holds bins
+// 8l .. 8l+7).
 template <typename T>
-__device__ int scan_down(const T *hist, T target, bool reach, T *above) {
-    T run = 0;
-    for (int b = 255; b >= 0; --b) {
-        const T next = run + hist[b];
-        if (reach ? next >= target : next > target) {
-            *above = run;
-            return b;
-        }
-        run = next;
+__device__ __forceinline__ void suffix_warp(const T *h, T *above, int lane) {
+    T s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += h[8 * lane + i];
+    T incl = s;  // sum over lanes >= this one
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const T t = __shfl_down_sync(0xffffffffu, incl, o);
+        if (lane + o < 32) incl += t;
     }
-    *above = run;
-    return -1;
+    T run = incl - s;  // exact: integers
+#pragma unroll
+    for (int i = 7; i >= 0; --i) {
+        above[8 * lane + i] = run;
+        run += h[8 * lane + i];
+    }
 }
 
-__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __grid_constant__ SampleArgs a) {
-    __shared__ float fh[256];
-    __shared__ unsigned int ch[256];
-    __shared__ unsigned long long red64[32];
-    __shared__ float redf[32];
-    __shared__ int s_bin, s_idx;
-    __shared__ float s_f0, s_f1;
-    __shared__ unsigned int s_u0;
-    const int row = blockIdx.x, tid = threadIdx.x, V = a.vocab;
-    const uint16_t *lg = static_cast<const uint16_t *>(a.logits) + (long long)row * a.row_stride;
+// One warp: the highest bin b >= lo where the running total from the top,
+// above[b] + h[b], reaches `target` (reach) or exceeds it; -1 if none. The
+// running total only grows downwards, so this is the first such bin from
+// the top.
+template <typename T>
+__device__ __forceinline__ int find_top(const T *h, const T *above, T target, bool reach, int lo, int lane) {
+    int best = -1;
+    for (int b = lane; b < 256; b += 32) {
+        if (b < lo) continue;
+        const T v = above[b] + h[b];
+        if (reach ? v >= target : v > target) best = max(best, b);
+    }
+    return warp_max_int(best);
+}
+// One warp: the lowest bin b >= lo with a nonzero count (256 if none).
+__device__ __forceinline__ int lowest_nonzero(const unsigned *c, int lo, int lane) {
+    int best = 256;
+    for (int b = lane; b < 256; b += 32)
+        if (b >= lo && c[b] != 0u) best = min(best, b);
+    return warp_min_int(best);
+}
 
-    // largest key, first index: max of (key << 32 | ~index)
-    unsigned long long best = 0;
-    for (int i = tid; i < V; i += kSampleThreads) {
-        const unsigned long long v = ((unsigned long long)key_of(lg[i]) << 32) | (0xFFFFFFFFu - (unsigned)i);
+__global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
+    sample_kernel(const __grid_constant__ SampleArgs a) {
+    extern __shared__ __align__(16) unsigned char dyn[];
+    Shared &sh = *reinterpret_cast<Shared *>(dyn);
+    uint16_t *skey = reinterpret_cast<uint16_t *>(dyn + sizeof(Shared));
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int row = blockIdx.x / kCtas, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int V = a.vocab;
+    const int per = (V + kCtas - 1) / kCtas;
+    const int start = min(V, rank * per), n = min(V, start + per) - start;
+    const uint16_t *lg = static_cast<const uint16_t *>(a.logits) + (long long)row * a.row_stride;
+    int stage = 0;  // the Pub buffer the next reduction writes
+
+    // ---- the slice as keys in shared memory; the largest key, first index
+    u64 best = 0;
+    for (int i = tid; i < n; i += kThreads) {
+        const uint32_t key = key_of(lg[start + i]);
+        skey[i] = (uint16_t)key;
+        const u64 v = ((u64)key << 32) | (0xFFFFFFFFu - (unsigned)(start + i));
         best = v > best ? v : best;
     }
-    best = block_reduce(best, [](unsigned long long x, unsigned long long y) { return x > y ? x : y; }, red64);
-    const uint32_t kmax = (uint32_t)(best >> 32);
-    const int argmax = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
+    best = warp_max64(best);
+    if (lane == 0) sh.red64[warp] = best;
+    __syncthreads();
+    if (warp == 0) {
+        u64 b = warp_max64(lane < kWarps ? sh.red64[lane] : 0ull);
+        if (lane == 0) sh.pub[stage].best = b;
+    }
+    cluster.sync();
+    if (warp == 0) {
+        const u64 o = lane < kCtas ? cluster.map_shared_rank(&sh.pub[stage], lane)->best : 0ull;
+        const u64 b = warp_max64(o);
+        if (lane == 0) sh.s_u[0] = b;
+    }
+    stage ^= 1;
+    __syncthreads();
+    const u64 gbest = sh.s_u[0];
+    const uint32_t kmax = (uint32_t)(gbest >> 32);
+    const int argmax = (int)(0xFFFFFFFFu - (uint32_t)(gbest & 0xFFFFFFFFu));
     if (a.mode == 0 || kmax == 0u) {  // greedy (a NaN first logit wins in the reference's loop); all NaN: 0
-        if (tid == 0) {
+        if (rank == 0 && tid == 0) {
             const uint16_t h0 = lg[0];
             const bool nan0 = (h0 & 0x7C00u) == 0x7C00u && (h0 & 0x03FFu) != 0;
             a.tokens[row] = nan0 || kmax == 0u ? 0 : argmax;
         }
+        cluster.sync();  // no CTA leaves while another may still read its shared memory
         return;
     }
     const float m = value_of(kmax);
     const float c = 1.4426950408889634f / a.temperature;  // exp((l - m) / T) = 2^((l - m) c)
-    auto weight = [&](uint32_t key) { return key == 0u ? 0.f : exp2f((value_of(key) - m) * c); };  // NaN: 0
-    if (tid == 0) a.tokens[row] = argmax;  // replaced below by the drawn token
+    // integer mass of a key: its weight in units of 2^-40 (NaN: 0)
+    auto fx = [&](uint32_t key) -> u64 {
+        return key == 0u ? 0ull : (u64)__float2ull_rn(exp2f((value_of(key) - m) * c) * kFx);
+    };
 
-    // ---- the candidate threshold: the lowest key kt of the candidates, the
-    // count (top-k) or mass (top-p) above it, and how many of its ties join
-    uint32_t kt;
-    float mass_gt;   // probability mass of keys > kt (unnormalised)
-    int need_eq;     // tokens with key == kt among the candidates (ascending index)
-    auto clear = [&]() {
-        for (int b = tid; b < 256; b += kSampleThreads) {
-            fh[b] = 0.f;
-            ch[b] = 0u;
+    // One histogram pass over the slice and its cluster reduction into
+    // sh.gmass / sh.gcnt and their suffix sums: the keys with high byte ==
+    // sel (sel < 0: every key), at their high byte (sel < 0) or low byte.
+    auto histogram = [&](int sel) {
+        for (int b = lane; b < 256; b += 32) {
+            sh.wmass[warp][b] = 0ull;
+            sh.wcnt[warp][b] = 0u;
+        }
+        __syncwarp();
+        for (int i = tid; i < n; i += kThreads) {
+            const uint32_t key = skey[i];
+            if (sel < 0 || (int)(key >> 8) == sel) {
+                const int b = sel < 0 ? (int)(key >> 8) : (int)(key & 0xFFu);
+                atomicAdd(&sh.wmass[warp][b], fx(key));
+                atomicAdd(&sh.wcnt[warp][b], 1u);
+            }
+        }
+        __syncthreads();
+        Pub &p = sh.pub[stage];
+        for (int b = tid; b < 256; b += kThreads) {
+            u64 ms = 0ull;
+            unsigned cs = 0u;
+            for (int w = 0; w < kWarps; ++w) {
+                ms += sh.wmass[w][b];
+                cs += sh.wcnt[w][b];
+            }
+            p.mass[b] = ms;
+            p.cnt[b] = cs;
+        }
+        cluster.sync();
+        for (int b = tid; b < 256; b += kThreads) {
+            u64 ms = 0ull;
+            unsigned cs = 0u;
+            for (int r = 0; r < kCtas; ++r) {
+                const Pub *o = cluster.map_shared_rank(&p, r);
+                ms += o->mass[b];
+                cs += o->cnt[b];
+            }
+            sh.gmass[b] = ms;
+            sh.gcnt[b] = cs;
+        }
+        stage ^= 1;
+        __syncthreads();
+        if (warp == 0) {
+            suffix_warp<u64>(sh.gmass, sh.amass, lane);
+            suffix_warp<unsigned>(sh.gcnt, sh.acnt, lane);
         }
         __syncthreads();
     };
-    if (a.mode == 1) {  // top-k (temperature: k = V)
-        const unsigned int k = (unsigned int)a.top_k;
-        clear();
-        for (int i = tid; i < V; i += kSampleThreads) atomicAdd(&ch[key_of(lg[i]) >> 8], 1u);
-        __syncthreads();
-        if (tid == 0) {
-            unsigned int above = 0;
-            s_bin = scan_down<unsigned int>(ch, k, true, &above);
-            s_u0 = above;
-        }
-        __syncthreads();
-        const int bh = s_bin;
-        const unsigned int c_above = s_u0;
-        __syncthreads();
-        clear();
-        for (int i = tid; i < V; i += kSampleThreads) {
-            const uint32_t key = key_of(lg[i]);
-            if ((int)(key >> 8) == bh) atomicAdd(&ch[key & 0xFFu], 1u);
-        }
-        __syncthreads();
-        if (tid == 0) {
-            unsigned int above = 0;
-            const int bl = scan_down<unsigned int>(ch, k - c_above, true, &above);
-            s_bin = (bh << 8) | bl;
-            s_u0 = k - c_above - above;  // ties of kt taken
-        }
-        __syncthreads();
-        kt = (uint32_t)s_bin;
-        need_eq = (int)s_u0;
-        float ms = 0.f;
-        for (int i = tid; i < V; i += kSampleThreads) {
-            const uint32_t key = key_of(lg[i]);
-            if (key > kt) ms += weight(key);
-        }
-        mass_gt = block_reduce(ms, [](float x, float y) { return x + y; }, redf);
-    } else {  // top-p: the smallest descending prefix reaching p of the total
-        clear();
-        float z = 0.f;
-        for (int i = tid; i < V; i += kSampleThreads) {
-            const uint32_t key = key_of(lg[i]);
-            const float w = weight(key);
-            z += w;
-            atomicAdd(&fh[key >> 8], w);
-        }
-        z = block_reduce(z, [](float x, float y) { return x + y; }, redf);
-        const float target = a.top_p * z;
-        if (tid == 0) {
-            float above = 0.f;
-            int b = scan_down<float>(fh, target, true, &above);
-            if (b < 0) {  // rounding: everything
-                b = 0;
-                above = 0.f;
-                while (b < 255 && fh[b] == 0.f) ++b;
-                above = 0.f;
-                for (int q = 255; q > b; --q) above += fh[q];
-            }
-            s_bin = b;
-            s_f0 = above;
-        }
-        __syncthreads();
-        const int bh = s_bin;
-        const float m_above = s_f0;
-        __syncthreads();
-        clear();
-        for (int i = tid; i < V; i += kSampleThreads) {
-            const uint32_t key = key_of(lg[i]);
-            if ((int)(key >> 8) == bh) {
-                atomicAdd(&fh[key & 0xFFu], weight(key));
-                atomicAdd(&ch[key & 0xFFu], 1u);
-            }
-        }
-        __syncthreads();
-        if (tid == 0) {
-            float above = 0.f;
-            int bl = scan_down<float>(fh, target - m_above, true, &above);
-            if (bl < 0) {  // rounding: the lowest key of the bin
-                bl = 0;
-                while (bl < 255 && ch[bl] == 0u) ++bl;
-                above = 0.f;
-                for (int q = 255; q > bl; --q) above += fh[q];
-            }
-            const uint32_t key = ((uint32_t)bh << 8) | (uint32_t)bl;
-            const float wt = weight(key);
-            const float gt = m_above + above;
-            int n = (int)ceilf((target - gt) / wt);
-            n = max(1, min(n, (int)ch[bl]));
-            s_bin = (int)key;
-            s_u0 = (unsigned int)n;
-            s_f1 = gt;
-        }
-        __syncthreads();
-        kt = (uint32_t)s_bin;
-        need_eq = (int)s_u0;
-        mass_gt = s_f1;
+
+    // ---- the candidate threshold kt (the lowest candidate key), the mass of
+    // the keys above it and how many of its ties join (lowest indices first)
+    histogram(-1);
+    for (int b = tid; b < 256; b += kThreads) {
+        sh.hmass1[b] = sh.gmass[b];
+        sh.amass1[b] = sh.amass[b];
     }
+    if (warp == 0) {
+        const u64 z = sh.amass[0] + sh.gmass[0];
+        int bh;
+        unsigned c_above = 0u;
+        u64 target = 0ull;
+        if (a.mode == 1) {  // top-k (temperature: k = V)
+            bh = find_top<unsigned>(sh.gcnt, sh.acnt, (unsigned)a.top_k, true, 0, lane);
+            if (bh < 0) bh = 0;  // (cannot happen: k <= V)
+            c_above = sh.acnt[bh];
+        } else {  // top-p: the smallest descending prefix reaching p of the total
+            target = (u64)((double)a.top_p * (double)z);
+            if (target == 0ull) target = 1ull;
+            bh = find_top<u64>(sh.gmass, sh.amass, target, true, 0, lane);
+            if (bh < 0) bh = lowest_nonzero(sh.gcnt, 0, lane);  // rounding: everything
+        }
+        if (lane == 0) {
+            sh.s_int[0] = bh;
+            sh.s_int[1] = (int)c_above;
+            sh.s_u[0] = target;
+        }
+    }
+    __syncthreads();
+    const int bh = sh.s_int[0];
+    const unsigned c_above1 = (unsigned)sh.s_int[1];
+    const u64 p_target = sh.s_u[0];
+    const u64 m_above1 = sh.amass1[bh];
+    __syncthreads();
+
+    histogram(bh);  // the low bytes of bin bh
+    if (warp == 0) {
+        int bl, neq;
+        if (a.mode == 1) {
+            const unsigned need = (unsigned)a.top_k - c_above1;
+            bl = find_top<unsigned>(sh.gcnt, sh.acnt, need, true, 0, lane);
+            if (bl < 0) bl = 0;  // (cannot happen: bin bh holds the k-th key)
+            neq = (int)(need - sh.acnt[bl]);
+        } else {
+            const u64 rest = p_target > m_above1 ? p_target - m_above1 : 0ull;
+            bl = find_top<u64>(sh.gmass, sh.amass, rest, true, 0, lane);
+            if (bl < 0) bl = lowest_nonzero(sh.gcnt, 0, lane);  // rounding: the lowest key of the bin
+            if (bl > 255) bl = 255;
+            const u64 gt = m_above1 + sh.amass[bl];
+            const u64 wkt = sh.gcnt[bl] ? sh.gmass[bl] / sh.gcnt[bl] : 0ull;  // one key's mass
+            const u64 need = p_target > gt ? p_target - gt : 0ull;
+            neq = wkt ? (int)min((u64)sh.gcnt[bl], (need + wkt - 1) / wkt) : (int)sh.gcnt[bl];
+            neq = max(1, neq);
+        }
+        if (lane == 0) {
+            sh.s_int[0] = (int)(((uint32_t)bh << 8) | (uint32_t)bl);
+            sh.s_int[1] = neq;
+            sh.s_u[0] = m_above1 + sh.amass[bl];  // mass above kt
+            sh.s_u[1] = sh.gcnt[bl] ? sh.gmass[bl] / sh.gcnt[bl] : 0ull;
+        }
+    }
+    __syncthreads();
+    const uint32_t kt = (uint32_t)sh.s_int[0];
+    const int need_eq = sh.s_int[1];
+    const u64 mass_gt = sh.s_u[0], wt = sh.s_u[1];
+    __syncthreads();
 
     // ---- the draw: target mass u * (mass above kt + its ties taken), walked
     // from the largest key down (equal keys by ascending index)
-    const float wt = weight(kt);
-    const float total = mass_gt + (float)need_eq * wt;
-    const float target = uniform_of(a.seed, a.step, row) * total;
-    uint32_t ks;      // the drawn key
-    int j;            // which of its ties (ascending index)
+    const u64 total = mass_gt + (u64)need_eq * wt;
+    const u64 target = (u64)((double)uniform_of(a.seed, a.step, row) * (double)total);
+    uint32_t ks;  // the drawn key
+    int j;        // which of its ties (ascending index)
     if (target >= mass_gt) {
         ks = kt;
-        j = wt > 0.f ? min((int)((target - mass_gt) / wt), need_eq - 1) : 0;
+        j = wt ? (int)min((u64)(need_eq - 1), (target - mass_gt) / wt) : 0;
     } else {
-        clear();
-        for (int i = tid; i < V; i += kSampleThreads) {
-            const uint32_t key = key_of(lg[i]);
-            if (key > kt) atomicAdd(&fh[key >> 8], weight(key));
+        // the high byte: bins above bh from the first pass, else bin bh
+        if (warp == 0) {
+            int sel = find_top<u64>(sh.hmass1, sh.amass1, target, false, bh + 1, lane);
+            if (sel < 0) sel = bh;
+            if (lane == 0) sh.s_int[0] = sel;
         }
         __syncthreads();
-        if (tid == 0) {
-            float above = 0.f;
-            int b = scan_down<float>(fh, target, false, &above);
-            if (b < 0) {  // rounding: the lowest bin with mass
-                b = 0;
-                while (b < 255 && fh[b] == 0.f) ++b;
-                above = 0.f;
-                for (int q = 255; q > b; --q) above += fh[q];
-            }
-            s_bin = b;
-            s_f0 = above;
-        }
+        const int bsel = sh.s_int[0];
+        const u64 m_above = sh.amass1[bsel];
         __syncthreads();
-        const int bh = s_bin;
-        const float m_above = s_f0;
-        __syncthreads();
-        clear();
-        for (int i = tid; i < V; i += kSampleThreads) {
-            const uint32_t key = key_of(lg[i]);
-            if (key > kt && (int)(key >> 8) == bh) {
-                atomicAdd(&fh[key & 0xFFu], weight(key));
-                atomicAdd(&ch[key & 0xFFu], 1u);
+        // the low byte: bin bh's keys above kt are in the second pass's
+        // histogram, another bin needs its own pass
+        if (bsel != bh) histogram(bsel);
+        if (warp == 0) {
+            const int lo_min = bsel == bh ? (int)(kt & 0xFFu) + 1 : 0;  // keys above kt only
+            const u64 rest = target > m_above ? target - m_above : 0ull;
+            int bl = find_top<u64>(sh.gmass, sh.amass, rest, false, lo_min, lane);
+            if (bl < 0) bl = min(255, lowest_nonzero(sh.gcnt, lo_min, lane));  // rounding: the lowest key
+            const u64 wk = sh.gcnt[bl] ? sh.gmass[bl] / sh.gcnt[bl] : 0ull;
+            const u64 in_bin = rest > sh.amass[bl] ? rest - sh.amass[bl] : 0ull;
+            if (lane == 0) {
+                sh.s_int[0] = (int)(((uint32_t)bsel << 8) | (uint32_t)bl);
+                sh.s_int[1] = wk ? (int)min((u64)max((int)sh.gcnt[bl] - 1, 0), in_bin / wk) : 0;
             }
         }
         __syncthreads();
-        if (tid == 0) {
-            float above = 0.f;
-            int bl = scan_down<float>(fh, target - m_above, false, &above);
-            if (bl < 0) {
-                bl = 0;
-                while (bl < 255 && ch[bl] == 0u) ++bl;
-                above = 0.f;
-                for (int q = 255; q > bl; --q) above += fh[q];
-            }
-            const uint32_t key = ((uint32_t)bh << 8) | (uint32_t)bl;
-            const float wk = weight(key);
-            s_bin = (int)key;
-            s_idx = wk > 0.f ? min((int)((target - m_above - above) / wk), (int)ch[bl] - 1) : 0;
-        }
+        ks = (uint32_t)sh.s_int[0];
+        j = sh.s_int[1];
         __syncthreads();
-        ks = (uint32_t)s_bin;
-        j = max(s_idx, 0);
     }
 
-    // ---- the j-th index (ascending) holding key ks: per-thread counts over
-    // contiguous chunks, an exclusive scan, then the owning thread's search
-    const int chunk = (V + kSampleThreads - 1) / kSampleThreads;
-    const int i0 = min(V, tid * chunk), i1 = min(V, i0 + chunk);
-    int cnt = 0;
-    for (int i = i0; i < i1; ++i) cnt += key_of(lg[i]) == ks;
-    // inclusive scan of cnt over the block (warp shuffles, then warp totals)
-    int incl = cnt;
-    const int lane = tid & 31, warp = tid >> 5;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-    }
-    __shared__ int wsum[32];
-    if (lane == 31) wsum[warp] = incl;
+    // ---- the j-th index (ascending) holding key ks: per-CTA counts, a prefix
+    // over the ranks, then a block-wide scan in the CTA that holds it
+    const int chunk = (n + kThreads - 1) / kThreads;
+    const int i0 = min(n, tid * chunk), i1 = min(n, i0 + chunk);
+    unsigned cnt = 0;
+    for (int i = i0; i < i1; ++i) cnt += skey[i] == ks;
+    const unsigned wcount = warp_sum(cnt);
+    if (lane == 0) sh.redu[warp] = wcount;
     __syncthreads();
     if (warp == 0) {
-        int w = wsum[lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, w, o);
-            if (lane >= o) w += t;
+        const unsigned t = warp_sum(lane < kWarps ? sh.redu[lane] : 0u);
+        if (lane == 0) sh.pub[stage].count = t;
+    }
+    cluster.sync();
+    if (warp == 0) {
+        const unsigned cr = lane < kCtas ? cluster.map_shared_rank(&sh.pub[stage], lane)->count : 0u;
+        const unsigned pre = warp_sum(lane < rank ? cr : 0u);
+        const unsigned total_ks = warp_sum(cr);
+        if (lane == 0) {
+            // j never passes the last index holding ks: the row always gets
+            // a drawn token
+            const int jj = min(j, (int)total_ks - 1);
+            const int local = jj - (int)pre;
+            sh.s_int[0] = local;
+            sh.s_int[1] = (int)total_ks;
+            sh.s_int[2] = total_ks > 0 && local >= 0 && local < (int)sh.pub[stage].count;
         }
-        wsum[lane] = w;  // inclusive over warps
     }
     __syncthreads();
-    // j never passes the last index holding ks (wsum[31] of them): rounding
-    // in the mass walk cannot leave the pre-set argmax standing in for a draw
-    j = min(j, wsum[31] - 1);
-    const int excl = incl - cnt + (warp > 0 ? wsum[warp - 1] : 0);
-    if (j >= excl && j < excl + cnt) {
-        int seen = excl;
-        for (int i = i0; i < i1; ++i)
-            if (key_of(lg[i]) == ks) {
-                if (seen == j) {
-                    a.tokens[row] = i;
-                    break;
-                }
-                ++seen;
+    const int jl = sh.s_int[0];
+    if (sh.s_int[1] == 0 && rank == 0 && tid == 0) a.tokens[row] = argmax;  // (cannot happen)
+    if (sh.s_int[2]) {  // this CTA holds the drawn index
+        unsigned incl = cnt;  // inclusive scan over the block: warp shuffles, then warp totals
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (lane == 31) sh.wpre[warp] = incl;
+        __syncthreads();
+        if (tid == 0) {
+            unsigned run = 0;
+            for (int w = 0; w < kWarps; ++w) {
+                const unsigned t = sh.wpre[w];
+                sh.wpre[w] = run;
+                run += t;
             }
+        }
+        __syncthreads();
+        const int excl = (int)(incl - cnt + sh.wpre[warp]);
+        if (jl >= excl && jl < excl + (int)cnt) {
+            int seen = excl;
+            for (int i = i0; i < i1; ++i)
+                if (skey[i] == ks) {
+                    if (seen == jl) {
+                        a.tokens[row] = start + i;
+                        break;
+                    }
+                    ++seen;
+                }
+        }
     }
+    cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 }  // namespace
 
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s) {
     if (a.rows <= 0) return cudaSuccess;
-    sample_kernel<<<a.rows, kSampleThreads, 0, s>>>(a);
+    if (a.vocab > kCtas * kMaxSlice || a.rows > (1 << 27)) return cudaErrorInvalidValue;
+    const int per = (a.vocab + kCtas - 1) / kCtas;
+    const int dyn = (int)(sizeof(Shared) + ((((size_t)per * 2) + 15) & ~size_t(15)));
+    // shared-memory opt-in per device, only ever raised (under one lock)
+    static std::mutex mu;
+    static std::map<int, int> opted;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        int &cur = opted[dev];
+        if (cur < dyn) {
+            e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+            if (e != cudaSuccess) return e;
+            cur = dyn;
+        }
+    }
+    sample_kernel<<<a.rows * kCtas, kThreads, dyn, s>>>(a);
     return cudaGetLastError();
 }
+
+int sample_max_vocab() { return kCtas * kMaxSlice; }
 
 }  // namespace tllm
