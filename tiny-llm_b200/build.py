@@ -30,7 +30,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-Wno-unused-parameter"]
 
-CU_SOURCES = ["kv_append.cu", "paged_decode.cu", "paged_prefill_tc.cu", "qkv_append.cu", "sampling.cu", "decode_static_scratch.cu"]
+CU_SOURCES = ["kv_append.cu", "paged_decode.cu", "paged_prefill_tc.cu", "qkv_append.cu", "qkv_append_tc.cu",
+              "sampling.cu", "decode_static_scratch.cu"]
 CPP_SOURCES = ["paged_kv.cpp"]
 # The C++ facade (tiny_llm::KVCacheManager) is compiled by its user, with the
 # user's include paths; the library itself exports only the C-ABI.
