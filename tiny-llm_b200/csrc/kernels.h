@@ -206,9 +206,9 @@ int qkv_rows_padded(int rows);  // the kernel's row tile for a launch of `rows` 
 cudaError_t launch_qkv_append(const QkvArgs &a, cudaStream_t s);
 // The tcgen05 variant (qkv_append_tc.cu): weight columns in tiles of 128
 // (Q, K and V each a multiple of 128 columns), group 32/64/128, weights
-// 16-byte aligned, ksplit <= 16. partial: fp32 [ksplit][columns / 128]
-// [qkv_tc_rows_padded][128] (every launch overwrites what it reads);
-// counters: [columns / 128], zero between launches. qkv_tc_split picks the
+// 16-byte aligned, ksplit <= 16. partial: fp32 [columns / 128]
+// [qkv_tc_rows_padded][128], counters: [columns / 128], both zero between
+// launches (the last CTA of a tile zeroes what it read). qkv_tc_split picks the
 // split of K for a launch of `rows` rows; false when no split keeps the
 // group accumulators within TMEM (the mma.sync kernel runs instead).
 bool qkv_tc_supported(int head_dim, int group, int nq, int nkv, int hidden);

@@ -1120,10 +1120,10 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
     if (tc && rows_last > 0 && num_seqs > tllm::kMaxQkvRows) tc = tc_plan(rows_last, &ks_last, &kchunk_last);
     size_t need;
     if (tc) {
-        // one fp32 slot per split and column tile
-        need = ks > 1 ? (size_t)ks * tiles128 * tllm::qkv_tc_rows_padded(rows_max) * 128 : 0;
+        // one fp32 accumulator per column tile
+        need = ks > 1 ? (size_t)tiles128 * tllm::qkv_tc_rows_padded(rows_max) * 128 : 0;
         if (ks_last > 1)
-            need = std::max(need, (size_t)ks_last * tiles128 * tllm::qkv_tc_rows_padded(rows_last) * 128);
+            need = std::max(need, (size_t)tiles128 * tllm::qkv_tc_rows_padded(rows_last) * 128);
     } else {
         // split-K: about three CTAs per SM (2 and 4 measured slower); a chunk's
         // activations stay under ~100 KB of shared memory
@@ -1387,6 +1387,9 @@ int tl_sync_check(tl_cache *c, tl_stream_t stream) {
         if (c->merge_counters)
             cudaMemset(c->merge_counters, 0,
                        (size_t)tllm::kMaxDecodeSeqs * c->cfg.num_kv_heads * sizeof(int));
+        // and a projection that stopped early, split-K sums and tickets
+        if (c->qkv_partial) cudaMemset(c->qkv_partial, 0, c->qkv_partial_floats * sizeof(float));
+        if (c->qkv_counters) cudaMemset(c->qkv_counters, 0, (size_t)c->qkv_counter_n * sizeof(int));
         std::string m = "device error word 0x" + [&] {
             char buf[16];
             std::snprintf(buf, sizeof buf, "%x", word);

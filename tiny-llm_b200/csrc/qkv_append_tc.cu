@@ -29,10 +29,10 @@
 // Each scale group is summed by the tensor core into its own fp32 TMEM
 // accumulator (fresh at the group's first k-step); the epilogue scales the
 // groups and adds them, sum_g s_g * (sum_k a_k w_k), as qkv_append.cu does.
-// Split-K: every CTA stores its fp32 partial sums from registers into its
-// own slot of the handle's scratch and arrives on the tile's counter with
-// release semantics; the last CTA to arrive (acquire) adds the slots in
-// split order, with several slots' loads in flight, rounds to fp16, rotates
+// Split-K: every CTA adds its fp32 partial sums into the tile's accumulator
+// in L2 (red.global.add.v4.f32) and arrives on the tile's counter with
+// release semantics; the last CTA to arrive (acquire) reads the total and
+// zeroes the accumulator for the next launch, rounds to fp16, rotates
 // Q and K pairs (d, d + D/2) by the RoPE table at the row's position (the
 // append kernel's rounding) and writes Q to q_out and K/V into their block
 // slots.
@@ -114,28 +114,38 @@ __device__ __forceinline__ void rope8(uint4 &x1v, uint4 &x2v, const float *c, co
     }
 }
 
-// NR (padded batch rows, UMMA N) columns of this thread's TMEM lane.
-template <int NR>
-__device__ __forceinline__ void tmem_ld_row(uint32_t taddr, float (&t)[NR]) {
-    uint32_t r[32];
-    if constexpr (NR == 16) {
-        asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                       "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-                       "=r"(r[14]), "=r"(r[15])
-                     : "r"(taddr));
-        ptx::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) t[i] = __uint_as_float(r[i]);
-    } else {
-#pragma unroll
-        for (int h = 0; h < NR / 32; ++h) {
-            ptx::tmem_ld32(taddr + 32 * h, r);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) t[32 * h + i] = __uint_as_float(r[i]);
-        }
-    }
+// 16 columns of this thread's TMEM lane, without waiting: the registers are
+// valid after tmem_wait_ld_into (which waits for every load in flight).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                   "=r"(r[15])
+                 : "r"(taddr));
+}
+// Waits for this thread's TMEM loads; the registers are operands so that no
+// use of them moves above the wait.
+__device__ __forceinline__ void tmem_wait_ld_into(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+// Orders later uses of r after the preceding (volatile) wait.
+__device__ __forceinline__ void regs_after_wait(uint32_t (&r)[16]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+__device__ __forceinline__ void red_add_v4(float *p, float4 v) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
 }
 
 template <int NR>
@@ -305,10 +315,9 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
     __syncwarp();  // the MMA and producer warps' lane 0 rejoins its warp
 
     // ---- epilogue: warps 0-3 read the group accumulators (thread = weight
-    // column; rows in chunks of up to 32) and sum s_g * acc_g. With split-K
-    // the sums go straight from registers to this CTA's slot (a warp stores
-    // 128 contiguous bytes per row); without, into an fp32 [NR][128] tile in
-    // the TMA ring (free: every load landed and every MMA completed) ----
+    // column; 16 rows at a time, three groups' TMEM loads per wait) and sum
+    // s_g * acc_g in group order into an fp32 [NR][128] tile in the TMA ring
+    // (free: every load landed and every MMA completed) ----
     float *sf = reinterpret_cast<float *>(sw);
     __half *sy = reinterpret_cast<__half *>(sw + NR * kTcM * 4);  // fp16 rows [NR][128]
     static_assert(64 * kTcM * 6 <= kNW * TcLayout<16>::kWStage, "epilogue staging outgrows the ring");
@@ -316,44 +325,53 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
     if (warp < kConvWarps) {
         ptx::named_barrier_sync(1, kConvThreads);  // every thread's scales landed
         const int nq4 = a.rows * (kTcM / 4);       // float4 chunks of the real rows
-        const int ntiles = (a.n[0] + a.n[1] + a.n[2]) / kTcM;
-        const long long slot = (long long)ntiles * NR * kTcM;  // floats per split slot
-        float *mine = a.ksplit > 1 ? a.partial + kc * slot + (long long)tile * NR * kTcM : nullptr;
         if (warp < 4) {
             const int col = 32 * warp + lane;
             bool done_ok = ptx::mbar_wait_bounded(done_u, 0u, kWaitNs);
             if (!done_ok && lane == 0) atomicOr(g.err, kErrWaitTimeout);
             done_ok = __all_sync(0xffffffffu, done_ok) && ok;
             ptx::tc_fence_after_sync();
-            constexpr int RC = 16;
+            constexpr int RC = 16, GB = 3;
+            const uint32_t tl = tbase + ((uint32_t)(32 * warp) << 16);
 #pragma unroll
             for (int rc = 0; rc < NR; rc += RC) {
                 float acc[RC];
 #pragma unroll
                 for (int r = 0; r < RC; ++r) acc[r] = 0.f;
                 if (done_ok) {
-                    for (int gi = 0; gi < ngroups; ++gi) {
-                        float tv[RC];
-                        tmem_ld_row<RC>(tbase + ((uint32_t)(32 * warp) << 16) + (uint32_t)(gi * NR + rc), tv);
-                        const float sv = __half2float(ssc[gi * kTcM + col]);
+                    for (int g0 = 0; g0 < ngroups; g0 += GB) {
+                        uint32_t v[GB][RC];
 #pragma unroll
-                        for (int r = 0; r < RC; ++r) acc[r] = fmaf(tv[r], sv, acc[r]);
+                        for (int u = 0; u < GB; ++u)
+                            if (g0 + u < ngroups) tmem_ld16(tl + (uint32_t)((g0 + u) * NR + rc), v[u]);
+                        tmem_wait_ld_into(v[0]);
+#pragma unroll
+                        for (int u = 1; u < GB; ++u) regs_after_wait(v[u]);
+#pragma unroll
+                        for (int u = 0; u < GB; ++u)
+                            if (g0 + u < ngroups) {
+                                const float sv = __half2float(ssc[(g0 + u) * kTcM + col]);
+#pragma unroll
+                                for (int r = 0; r < RC; ++r) acc[r] = fmaf(__uint_as_float(v[u][r]), sv, acc[r]);
+                            }
                     }
                 }
-                if (mine) {
 #pragma unroll
-                    for (int r = 0; r < RC; ++r)
-                        if (rc + r < a.rows) __stcg(mine + (rc + r) * kTcM + col, acc[r]);
-                } else {
-#pragma unroll
-                    for (int r = 0; r < RC; ++r) sf[(rc + r) * kTcM + col] = acc[r];
-                }
+                for (int r = 0; r < RC; ++r) sf[(rc + r) * kTcM + col] = acc[r];
             }
         }
         ptx::named_barrier_sync(1, kConvThreads);
         if (a.ksplit > 1) {
-            // the arrival releases this CTA's slot (the barrier orders the
-            // other warps' stores before it); the last arrival acquires all
+            // add this CTA's sums into the tile's fp32 accumulator in L2, then
+            // arrive on the tile's counter: the arrival releases the adds (the
+            // barrier orders the other warps' before it); the last arrival
+            // acquires them all, reads the total and leaves zeros behind
+            float *tacc = a.partial + (long long)tile * NR * kTcM;
+            for (int i = threadIdx.x; i < nq4; i += kConvThreads) {
+                const float4 v = *reinterpret_cast<const float4 *>(sf + 4 * i);
+                red_add_v4(tacc + 4 * i, v);
+            }
+            ptx::named_barrier_sync(1, kConvThreads);
             if (threadIdx.x == 0) {
                 const int prev = ptx::atom_add_acq_rel_gpu(&a.counters[tile], 1);
                 s_last = prev == a.ksplit - 1;
@@ -361,40 +379,18 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
             }
             ptx::named_barrier_sync(1, kConvThreads);
             if (s_last) {
-                // add the slots in split order; every thread has kU slots'
-                // loads in flight at a time
                 constexpr int kPer = NR / 8;  // float4 chunks per thread (NR * 32 over 256 threads)
-                constexpr int kU = NR <= 16 ? 6 : (NR <= 32 ? 2 : 1);
-                const float4 *base = reinterpret_cast<const float4 *>(a.partial + (long long)tile * NR * kTcM);
                 float4 t[kPer];
 #pragma unroll
-                for (int j = 0; j < kPer; ++j) t[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int q0 = 0; q0 < a.ksplit; q0 += kU) {
-                    float4 v[kU][kPer];
-#pragma unroll
-                    for (int u = 0; u < kU; ++u)
-#pragma unroll
-                        for (int j = 0; j < kPer; ++j) {
-                            const int i = threadIdx.x + kConvThreads * j;
-                            v[u][j] = (q0 + u < a.ksplit && i < nq4) ? __ldcg(base + (q0 + u) * (slot / 4) + i)
-                                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
-#pragma unroll
-                    for (int u = 0; u < kU; ++u)
-                        if (q0 + u < a.ksplit) {
-#pragma unroll
-                            for (int j = 0; j < kPer; ++j) {
-                                t[j].x += v[u][j].x;
-                                t[j].y += v[u][j].y;
-                                t[j].z += v[u][j].z;
-                                t[j].w += v[u][j].w;
-                            }
-                        }
+                for (int j = 0; j < kPer; ++j) {
+                    const int i = threadIdx.x + kConvThreads * j;
+                    t[j] = i < nq4 ? __ldcg(reinterpret_cast<const float4 *>(tacc) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
                 for (int j = 0; j < kPer; ++j) {
                     const int i = threadIdx.x + kConvThreads * j;
                     if (i < nq4) {
+                        __stcg(reinterpret_cast<float4 *>(tacc) + i, make_float4(0.f, 0.f, 0.f, 0.f));
                         __half2 *dst = reinterpret_cast<__half2 *>(sy + 4 * i);
                         dst[0] = __floats2half2_rn(t[j].x, t[j].y);
                         dst[1] = __floats2half2_rn(t[j].z, t[j].w);
