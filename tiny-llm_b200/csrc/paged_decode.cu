@@ -392,12 +392,60 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         ptx::fence_barrier_init();
     }
     __syncwarp();
+    // ---- producer side: lane j of a batch describes item (base + j) ------
+    // The item positions come from the launch parameters alone, so the first
+    // two batches are placed before the wait for the previous grid; their
+    // block-table reads (which a previous kernel may have written) follow
+    // the wait, both in flight together.
+    struct BatchPos {
+        long long bt_off;  // block-table entry of the item's tile
+        int kvh, sub;
+        bool real;         // this lane's slot is a real tile of the range
+    };
+    struct Batch {
+        int bid, kvh, sub;
+        unsigned real;  // ballot: lanes whose slot is a real tile of this range
+    };
+    auto place_batch = [&](long long base) {
+        BatchPos r{0, 0, 0, false};
+        const long long w = base + lane;
+        if (w < we) {
+            const ItemPos p = locate(a, w);
+            if (p.tile() >= 0) {
+                const int tok0 = p.tile() * kTile;
+                r.real = true;
+                r.bt_off = (long long)a.slot[p.b] * g.bt_stride + tok0 / BS;
+                r.kvh = p.kvh;
+                r.sub = tok0 % BS;
+            }
+        }
+        return r;
+    };
+    auto finish_batch = [&](const BatchPos &pos, int bid) {
+        Batch r{0, pos.kvh, pos.sub, 0u};
+        if (pos.real) {
+            if (bid < 0 || bid >= g.num_blocks) {
+                atomicOr(g.err, kErrBlockRange);
+                bid = 0;  // stay in bounds; the call reports the error
+            }
+            r.bid = bid;
+        }
+        r.real = __ballot_sync(0xffffffffu, pos.real);
+        return r;
+    };
+    auto load_batch = [&](long long base) {
+        const BatchPos pos = place_batch(base);
+        return finish_batch(pos, pos.real ? __ldg(g.block_tables + pos.bt_off) : 0);
+    };
+    const BatchPos pos0 = place_batch(ws), pos1 = place_batch(ws + 32);
+
     // Programmatic dependent launch. With the in-kernel merge the dependent is
     // the next decode, whose CTAs only fit as ours retire: it may begin
     // launching now. With the merge pass the dependent is that pass, whose
     // CTAs would sit on our SMs and take issue slots while they wait: it is
     // released only once this CTA's loads are done. This kernel reads nothing
-    // from global memory before the previous grid has completed.
+    // from global memory before the previous grid has completed (only the
+    // parameter-only placement of its first items comes before the wait).
     const bool early_trigger = a.counters != nullptr;
     if (early_trigger) ptx::griddep_launch_dependents();
     ptx::griddep_wait();
@@ -406,37 +454,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     const long long layer_k_row = (long long)(a.layer * 2 + 0) * g.num_blocks;
     const long long layer_v_row = (long long)(a.layer * 2 + 1) * g.num_blocks;
 
-    // ---- producer side: lane j of a batch describes item (base + j) ------
-    struct Batch {
-        int bid, kvh, sub;
-        unsigned real;  // ballot: lanes whose slot is a real tile of this range
-    };
-    auto load_batch = [&](long long base) {
-        Batch r{0, 0, 0, 0u};
-        const long long w = base + lane;
-        bool is_real = false;
-        if (w < we) {
-            const ItemPos p = locate(a, w);
-            if (p.tile() >= 0) {
-                is_real = true;
-                const int tok0 = p.tile() * kTile;
-                const int slot = a.slot[p.b];
-                int bid = __ldg(g.block_tables + (long long)slot * g.bt_stride + tok0 / BS);
-                if (bid < 0 || bid >= g.num_blocks) {
-                    atomicOr(g.err, kErrBlockRange);
-                    bid = 0;  // stay in bounds; the call reports the error
-                }
-                r.bid = bid;
-                r.kvh = p.kvh;
-                r.sub = tok0 % BS;
-            }
-        }
-        r.real = __ballot_sync(0xffffffffu, is_real);
-        return r;
-    };
     long long cur_base = ws;
-    Batch cur = load_batch(ws);
-    Batch nxt = load_batch(ws + 32);
+    const int bid0 = pos0.real ? __ldg(g.block_tables + pos0.bt_off) : 0;
+    const int bid1 = pos1.real ? __ldg(g.block_tables + pos1.bt_off) : 0;
+    Batch cur = finish_batch(pos0, bid0);
+    Batch nxt = finish_batch(pos1, bid1);
     int issued = 0;  // real tiles issued; stage = issued % kNS
     // Issues the next real tile of the range (uniform across the warp);
     // false when the range has none left.
