@@ -1311,7 +1311,7 @@ def main():
                                "strategy": "top-p 0.9, T 0.8 (do_sample)",
                                "l2": "8 MB of logits, re-read per pass from L2 (one read from HBM)"},
                     "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                                 "frac": round(achieved / peak, 4), "traffic": None,
+                                 "frac": round(achieved / peak, 4), "traffic": launch_traffic("smp"),
                                  "kernel": "sample_kernel (a cluster of 8 CTAs per row, the row's slice of keys in shared memory)",
                                  "note": "one HBM read of the logits; bound by ~10 cluster-wide histogram reductions per row, not by HBM",
                                  "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},
@@ -1344,7 +1344,7 @@ def main():
                     "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                                  "frac": round(achieved / peak, 4), "traffic": launch_traffic("qkv"),
                                  "algorithmic_bytes_per_launch": res["k_bytes"],
-                                 "kernel": "qkv_append_kernel (W8A16 mma.sync, split-K, fused append)",
+                                 "kernel": "qkv_append_tc_kernel (W8A16 on tcgen05, fp16 weights in TMEM, split-K, fused append)",
                                  "us_per_launch": round(res["k_ms"] * 1e3, 2),
                                  "timed_as": "the step's launches replayed from a CUDA graph (kernel time without host calls)",
                                  "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"},
