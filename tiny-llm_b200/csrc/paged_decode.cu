@@ -388,6 +388,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     const uint32_t bar_u32 = ptx::smem_u32(bars);
 
     if (lane == 0) {
+        ptx::prefetch_tensormap(&tmap);  // a launch parameter: safe before the wait below
         for (int s = 0; s < C::kNS; ++s) ptx::mbar_init(bar_u32 + 8 * s, 1);
         ptx::fence_barrier_init();
     }

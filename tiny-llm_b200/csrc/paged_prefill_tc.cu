@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int ntiles = (pos0 + q_last) / kTcKeys + 1;  // keys [0, position of the last query]
 
     if (threadIdx.x == 0) {
+        ptx::prefetch_tensormap(&tmap);
         for (int s = 0; s < C::kNS; ++s) {
             ptx::mbar_init(full_u + 8 * s, 1);
             ptx::mbar_init(empty_u + 8 * s, 1);

@@ -190,6 +190,12 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint
         : "memory");
 }
 
+// Brings a tensor map (a kernel parameter) into the TMA unit's descriptor
+// cache ahead of its first use.
+__device__ __forceinline__ void prefetch_tensormap(const void *tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
 // 2-D tiled TMA prefetch global -> L2 (no shared memory, no barrier). L2 is
 // the device's point of coherence, so a later load still sees any write
 // made after the prefetch.

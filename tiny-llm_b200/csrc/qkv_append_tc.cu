@@ -193,6 +193,8 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
         // before this one on the stream may still run (programmatic launch):
         // a prefetch only warms L2, the loads themselves come after
         // griddepcontrol.wait like every other read.
+        ptx::prefetch_tensormap(&maps.w[m]);
+        ptx::prefetch_tensormap(&maps.x);
         for (int blk = 0; blk < nblk; ++blk) ptx::tma_prefetch_2d(&maps.w[m], col0, k0 + blk * kBlk);
     }
     if (threadIdx.x == 0) {
