@@ -281,6 +281,9 @@ def _close_f16_rows(got, exp, what):
     (64, 8, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 64, 384, 64),
     (128, 4, 16, False, T.TL_LAYOUT_TOKEN_MAJOR, 70, 256, 32),
     (128, 4, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 33, 512, 16),
+    (128, 2, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 40, 4096, 32),
+    (128, 2, 16, True, T.TL_LAYOUT_HEAD_MAJOR, 50, 4096, 128),
+    (128, 4, 32, False, T.TL_LAYOUT_TOKEN_MAJOR, 20, 4096, 64),
 ])
 def test_project_qkv_append(D, G, bs, rope, layout, B, hidden, group):
     """Fused W8A16 Q/K/V projection of one decode token per sequence
@@ -289,7 +292,10 @@ def test_project_qkv_append(D, G, bs, rope, layout, B, hidden, group):
     restatement of the reference matmul rounded to fp16 (then rotated at
     that position when the cache rotates on append); every earlier row of
     the pool is untouched. B = 70 runs as two launches. Group 16 runs the
-    mma.sync kernel, the other groups the tcgen05 kernel."""
+    mma.sync kernel, the other groups the tcgen05 kernel, except where no
+    split of K keeps the group accumulators within TMEM (group 32 with 40
+    rows of hidden 4096), which falls back to the mma.sync kernel; hidden
+    4096 with groups 64 and 128 runs the tcgen05 kernel at 32 and 64 rows."""
     import torch
     Hkv = 2
     Hq = Hkv * G

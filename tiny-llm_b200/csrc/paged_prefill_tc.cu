@@ -38,8 +38,9 @@
 // (MN-major, rows = keys), all with the 128-byte swizzle; P is the A
 // operand of P V straight from TMEM. fp16 in, fp32 accumulate. CTAs are
 // numbered KV head fastest, so the CTAs in flight spread over the heads
-// instead of all reading one head's K/V. Every wait is bounded; TMEM is
-// freed on every path.
+// instead of all reading one head's K/V, and query blocks last-first, so
+// the launch ends on the blocks with the fewest keys. Every wait is
+// bounded; TMEM is freed on every path.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -129,7 +130,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const PoolGeom &g = a.g;
     const int H = g.num_kv_heads, G = a.group, Gp = a.group_pad, Hq = H * G, BS = g.block_size;
     const int lin = (int)(blockIdx.x + blockIdx.y * gridDim.x);
-    const int kvh = lin % H, xq = lin / H;  // KV head fastest
+    // KV head fastest; query blocks from the last to the first, so that the
+    // causal blocks with the most keys start first and the last wave holds
+    // the lightest ones (a sequence's early query blocks)
+    const int kvh = lin % H, xq = a.cta_prefix[a.nseq] - 1 - lin / H;
 
     int lo = 0, hi = a.nseq - 1;  // sequence of this CTA: largest b with cta_prefix[b] <= xq
     while (lo < hi) {
