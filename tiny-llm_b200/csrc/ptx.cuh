@@ -223,6 +223,22 @@ __device__ __forceinline__ void tmem_st_16x256b(uint32_t taddr, uint32_t r0, uin
                  : "memory");
 }
 
+// Bulk reduction shared -> global: dst[i] += src[i] for `bytes` / 4 fp32
+// values (both 16-byte aligned, bytes a multiple of 16), in the async
+// proxy; bulk_wait_all() waits until it is complete.
+__device__ __forceinline__ void bulk_reduce_add_f32(float *dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
+                 "r"(src_smem), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's async-proxy global writes before its later
+// generic-proxy operations.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Device-scope fetch-and-add with acquire-release semantics (the arrival of
 // a split-K CTA: its partial sums before, the last arrival's reads after).
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int *p, int v) {

@@ -30,7 +30,8 @@
 // accumulator (fresh at the group's first k-step); the epilogue scales the
 // groups and adds them, sum_g s_g * (sum_k a_k w_k), as qkv_append.cu does.
 // Split-K: every CTA adds its fp32 partial sums into the tile's accumulator
-// in L2 (red.global.add.v4.f32) and arrives on the tile's counter with
+// in L2 (one bulk reduction of its staged rows, cp.reduce.async.bulk .add.f32)
+// and arrives on the tile's counter with
 // release semantics; the last CTA to arrive (acquire) reads the total and
 // zeroes the accumulator for the next launch, rounds to fp16, rotates
 // Q and K pairs (d, d + D/2) by the RoPE table at the row's position (the
@@ -140,11 +141,6 @@ __device__ __forceinline__ void regs_after_wait(uint32_t (&r)[16]) {
                    "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
                    "+r"(r[15])
                  :
-                 : "memory");
-}
-
-__device__ __forceinline__ void red_add_v4(float *p, float4 v) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                  : "memory");
 }
 
@@ -364,17 +360,19 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
         }
         ptx::named_barrier_sync(1, kConvThreads);
         if (a.ksplit > 1) {
-            // add this CTA's sums into the tile's fp32 accumulator in L2, then
-            // arrive on the tile's counter: the arrival releases the adds (the
-            // barrier orders the other warps' before it); the last arrival
+            // add this CTA's sums into the tile's fp32 accumulator in L2 with
+            // one bulk reduction of the staged rows (whole lines at L2, not
+            // per-thread atomics), wait for it, then arrive on the tile's
+            // counter: the arrival releases the adds; the last arrival
             // acquires them all, reads the total and leaves zeros behind
             float *tacc = a.partial + (long long)tile * NR * kTcM;
-            for (int i = threadIdx.x; i < nq4; i += kConvThreads) {
-                const float4 v = *reinterpret_cast<const float4 *>(sf + 4 * i);
-                red_add_v4(tacc + 4 * i, v);
-            }
+            ptx::fence_proxy_async_smem();  // sf's generic writes before the bulk copy reads them
             ptx::named_barrier_sync(1, kConvThreads);
             if (threadIdx.x == 0) {
+                ptx::bulk_reduce_add_f32(tacc, ptx::smem_u32(sf), (uint32_t)(nq4 * 16));
+                ptx::bulk_commit();
+                ptx::bulk_wait_all();
+                ptx::fence_proxy_async_global();
                 const int prev = ptx::atom_add_acq_rel_gpu(&a.counters[tile], 1);
                 s_last = prev == a.ksplit - 1;
                 if (s_last) a.counters[tile] = 0;  // ready for the next launch
