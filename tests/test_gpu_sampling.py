@@ -124,3 +124,28 @@ def test_draws_with_many_ties_at_the_cutoff(kw):
         assert int(got[r]) in ok, f"row {r}: {got[r]} not in {sorted(ok)[:8]}"
         argmax_hits += int(got[r]) == S.greedy(xr)
     assert argmax_hits < rows // 2
+
+
+@pytest.mark.parametrize("V", [65537, 524287, 524288])
+def test_largest_vocabularies(V):
+    """Rows split over the cluster's 8 slices just past one slice (65537)
+    and at the largest supported vocabulary (8 x 65536): greedy bit for bit
+    (the maximum placed in the first and in the last key), and top-k/top-p
+    draws at the oracle's uniform."""
+    rows = 6
+    rng = np.random.default_rng(V)
+    x = np.round(rng.normal(0, 3, (rows, V)) * 8) / 8
+    x[0, V - 1] = 40.0
+    x[1, 0] = 40.0
+    lg = O.f32_to_f16(x.astype(np.float32))
+    got = _run(lg, rows, V, V)
+    exp = [S.greedy(O.f16_to_f32(lg[r]).astype(np.float64)) for r in range(rows)]
+    assert list(got) == exp
+    assert exp[0] == V - 1 and exp[1] == 0
+    kw = dict(temperature=0.8, top_k=50, top_p=0.9)
+    seed, step = 77, 3
+    got = _run(lg, rows, V, V, do_sample=True, seed=seed, step=step, **kw)
+    for r in range(rows):
+        xr = O.f16_to_f32(lg[r]).astype(np.float64)
+        ok = S.window(xr, True, seed=seed, step=step, row=r, tol=1e-4, **kw)
+        assert int(got[r]) in ok, f"row {r}: {got[r]} not in {sorted(ok)[:8]}"
