@@ -8,8 +8,9 @@
 // columns come in tiles of 128 and the scale groups hold 32, 64 or 128 rows.
 //
 // The weights are the M side of one UMMA per 16 rows of K (M = 128 weight
-// columns per CTA, MN-major A operand), the batch rows the N side (N = 16,
-// 32 or 64, K-major B operand), so the tensor core reads every weight once
+// columns per CTA, A operand in TMEM, K-major), the batch rows the N side
+// (N = 16, 32 or 64, K-major B operand in shared memory), so the tensor
+// core reads every weight once
 // and the math costs little next to the weight stream. Per CTA (a column
 // tile x a K-chunk, split-K over the grid), in 64-row blocks:
 //   warp 9     the producer: TMA loads of the block's int8 weight tile
@@ -30,10 +31,10 @@
 // accumulator (fresh at the group's first k-step); the epilogue scales the
 // groups and adds them, sum_g s_g * (sum_k a_k w_k), as qkv_append.cu does.
 // Split-K: every CTA adds its fp32 partial sums into the tile's accumulator
-// in L2 (one bulk reduction of its staged rows, cp.reduce.async.bulk .add.f32)
-// and arrives on the tile's counter with
-// release semantics; the last CTA to arrive (acquire) reads the total and
-// zeroes the accumulator for the next launch, rounds to fp16, rotates
+// in L2 (one bulk reduction of its staged rows, cp.reduce.async.bulk
+// .add.f32) and arrives on the tile's counter with release semantics; the
+// last CTA to arrive (acquire) reads the total and zeroes the accumulator
+// for the next launch, rounds to fp16, rotates
 // Q and K pairs (d, d + D/2) by the RoPE table at the row's position (the
 // append kernel's rounding) and writes Q to q_out and K/V into their block
 // slots.
