@@ -680,6 +680,15 @@ def run_qkv(cfg, args, world, rank, local):
     gen = torch.Generator(device="cuda")
     gen.manual_seed(args.seed * 7919 + rank)
     ws = _qkv_weights(cfg, L, gen)
+    packed = args.qkv_weights == "packed"
+    if packed:  # once, as at model load: the tile-blocked copy replaces the row-major one
+        for layer in ws:
+            for j in (0, 2, 4):
+                pk = torch.empty_like(layer[j])
+                T.pack_qkv_weight(layer[j].data_ptr(), hidden, layer[j].shape[1], pk.data_ptr(), sp)
+                layer[j] = pk
+        torch.cuda.synchronize()
+    project = cache.project_qkv_append_packed if packed else cache.project_qkv_append
     x = torch.randn((L, B, hidden), dtype=torch.float16, device="cuda", generator=gen)
     q = torch.empty((L, B, Hq * D), dtype=torch.float16, device="cuda")
 
@@ -687,9 +696,8 @@ def run_qkv(cfg, args, world, rank, local):
         s = s or sp
         for l in range(L):
             w = ws[l]
-            cache.project_qkv_append(l, x[l].data_ptr(), hidden, w[0].data_ptr(), w[1].data_ptr(),
-                                     w[2].data_ptr(), w[3].data_ptr(), w[4].data_ptr(), w[5].data_ptr(),
-                                     group, sids, q[l].data_ptr(), s)
+            project(l, x[l].data_ptr(), hidden, w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(),
+                    w[3].data_ptr(), w[4].data_ptr(), w[5].data_ptr(), group, sids, q[l].data_ptr(), s)
 
     for _ in range(args.warmup):
         step()
@@ -749,9 +757,11 @@ def run_qkv(cfg, args, world, rank, local):
         import numpy as np
         import oracle as O
         xs = x[0].cpu().numpy().view(np.uint16)
+        cw = [(torch.randint(-127, 128, (hidden, n), dtype=torch.int8).numpy(),
+               ws[0][2 * j + 1].cpu().numpy().view(np.uint16)) for j, n in enumerate((Hq * D, Hkv * D, Hkv * D))]
         t0 = time.perf_counter()
-        for j in range(3):
-            O.w8a16_matmul(xs, ws[0][2 * j].cpu().numpy(), ws[0][2 * j + 1].cpu().numpy().view(np.uint16), group)
+        for w, sc in cw:
+            O.w8a16_matmul(xs, w, sc, group)
         el = time.perf_counter() - t0
         cpu = {"value": round(qkv_weight_bytes(cfg) / el / 1e9, 3), "unit": "GB/s",
                "cores": os.cpu_count() or 1, "kind": "port",
@@ -1138,6 +1148,9 @@ def main():
                     help="fused: one append of every layer's new token, then decode per layer; "
                          "layer: per layer, append that layer's token then decode with RoPE on Q "
                          "(the TransformerLayer::attention flow, tl_attention_step)")
+    ap.add_argument("--qkv-weights", choices=["packed", "reference"], default="packed",
+                    help="qkv config: weights repacked once by tl_qkv_pack_weight (tl_project_qkv_append_packed), "
+                         "or read in the reference's QuantizedWeight layout (tl_project_qkv_append)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--layers", type=int, default=0,
                     help="override the config's layer count (small profiling cases; "
@@ -1340,6 +1353,9 @@ def main():
                     "config": dict({k: v for k, v in base_config.items() if k not in ("flow",)},
                                    global_batch=res["B"] * world, hidden=cfg["hidden"], group_size=cfg["group"],
                                    step="per layer: Q/K/V projections of every sequence's token, K/V into the pool, Q rotated",
+                                   weights=("tile-blocked copies made once at setup by tl_qkv_pack_weight "
+                                            "(tl_project_qkv_append_packed)" if args.qkv_weights == "packed" else
+                                            "the reference's QuantizedWeight layout (tl_project_qkv_append)"),
                                    l2="839 MB of weights per step, each layer's read once; no flush needed"),
                     "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                                  "frac": round(achieved / peak, 4), "traffic": launch_traffic("qkv"),

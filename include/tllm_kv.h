@@ -220,6 +220,25 @@ int tl_project_qkv_append(tl_cache *cache, int layer, const void *x, int hidden,
                           const void *sq, const int8_t *wk, const void *sk, const int8_t *wv, const void *sv,
                           int group_size, const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream);
 
+/* Weight repacking for tl_project_qkv_append_packed, done once at model load
+ * (no reference counterpart: the reference reads QuantizedWeight as stored).
+ * w: int8 [hidden][n] row-major as above; packed: a device buffer of the same
+ * hidden * n bytes, not overlapping w. Layout: column tile t (128 columns),
+ * 64-row block b is 8192 contiguous bytes at (t * hidden / 64 + b) * 8192,
+ * its row r's 16-byte chunk c at r * 128 + (c ^ (r % 8)) * 16. hidden and n
+ * multiples of 128, both pointers 16-byte aligned. Asynchronous on `stream`.
+ * No handle: errors are read with tl_last_error(NULL). */
+int tl_qkv_pack_weight(const int8_t *w, int hidden, int n, int8_t *packed, tl_stream_t stream);
+
+/* tl_project_qkv_append with wq/wk/wv packed by tl_qkv_pack_weight (the
+ * scales as before): the same outputs, bit for bit, with every weight read
+ * a contiguous 8 KB copy. Only for the shapes the tcgen05 kernel takes: Q,
+ * K and V widths multiples of 128, group_size 32/64/128; TL_ERR_UNSUPPORTED
+ * otherwise. */
+int tl_project_qkv_append_packed(tl_cache *cache, int layer, const void *x, int hidden, const int8_t *wq,
+                                 const void *sq, const int8_t *wk, const void *sk, const int8_t *wv, const void *sv,
+                                 int group_size, const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream);
+
 /* Next-token sampling on the device for `rows` rows of fp16 logits
  * (row_stride elements apart; 0 shares one row), replacing the host round
  * trip of InferenceEngine::sampleFromHidden (reference

@@ -336,3 +336,90 @@ def test_project_qkv_append(D, G, bs, rope, layout, B, hidden, group):
         _close_f16_rows(v[lens[i]], ev[i], f"V row of seq {sid}")
         assert r.cache.get_seq_len(sid) == lens[i]  # the length does not advance
     r.check_pool_bit_exact()  # the prefix rows of every layer are untouched
+
+
+def _pack_layout(w):
+    """numpy restatement of tl_qkv_pack_weight's layout: column tile t,
+    64-row block b is 8192 bytes at (t * K / 64 + b) * 8192, row r's 16-byte
+    chunk c at r * 128 + (c ^ (r % 8)) * 16."""
+    K, n = w.shape
+    t = w.reshape(K // 64, 64, n // 128, 8, 16).transpose(2, 0, 1, 3, 4)  # [tile][block][row][chunk][16]
+    rows = np.arange(64)[:, None]
+    src_chunk = np.arange(8)[None, :] ^ (rows & 7)  # position p holds chunk p ^ (r % 8)
+    return np.ascontiguousarray(t[:, :, rows, src_chunk, :]).reshape(-1)
+
+
+@pytest.mark.parametrize("D,G,bs,rope,layout,B,hidden,group", [
+    (128, 4, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 5, 512, 32),
+    (64, 8, 16, True, T.TL_LAYOUT_TOKEN_MAJOR, 64, 384, 64),
+    (128, 4, 16, False, T.TL_LAYOUT_TOKEN_MAJOR, 70, 256, 32),
+    (128, 2, 16, True, T.TL_LAYOUT_HEAD_MAJOR, 50, 4096, 128),
+    (128, 4, 32, False, T.TL_LAYOUT_TOKEN_MAJOR, 20, 4096, 64),
+])
+def test_project_qkv_append_packed(D, G, bs, rope, layout, B, hidden, group):
+    """Weights repacked on the device by tl_qkv_pack_weight equal the numpy
+    restatement of the tile-blocked layout byte for byte; the projection
+    from them (tl_project_qkv_append_packed) writes Q and every sequence's
+    K/V row within two fp16 units of the oracle, as tl_project_qkv_append
+    does from the reference layout, and leaves every other pool row
+    untouched. (Split-K partial sums meet in L2 in arrival order, so two
+    runs of either entry may differ in the last bit; the oracle is the
+    check.) B = 70 runs as two launches; hidden 4096 runs 16-way split-K."""
+    import torch
+    Hkv = 2
+    Hq = Hkv * G
+    L = 2
+    r = Run.create(L=L, Hq=Hq, Hkv=Hkv, D=D, bs=bs, max_seq_len=160, max_batch=B, rope=rope,
+                   layout=layout, permute_seed=9)
+    lens = [(5 * i + 2) % 89 for i in range(B)]
+    sids = [r.allocate(160) for _ in range(B)]
+    for i, (sid, P) in enumerate(zip(sids, lens)):
+        if P:
+            r.prefill(sid, P, seed=500 + i)
+    x = O.normal_f16((B, hidden), 91 + B)
+    ws = [_qkv_weights(hidden, nc, group, 11 + j) for j, nc in enumerate((Hq * D, Hkv * D, Hkv * D))]
+    xd = to_dev(x)
+    wd = [torch.from_numpy(w.copy()).cuda() for w, _ in ws]
+    sd = [to_dev(sc) for _, sc in ws]
+    packed = [torch.empty_like(w) for w in wd]
+    for w, p in zip(wd, packed):
+        T.pack_qkv_weight(w.data_ptr(), hidden, w.shape[1], p.data_ptr())
+    torch.cuda.synchronize()
+    for (w, _), p in zip(ws, packed):
+        assert np.array_equal(p.cpu().numpy().reshape(-1), _pack_layout(w)), "packed layout differs"
+    del wd
+    layer = 1
+    qd = torch.full((B, Hq * D), 0x7e00, dtype=torch.int16, device="cuda")
+    r.cache.project_qkv_append_packed(layer, xd.data_ptr(), hidden, packed[0].data_ptr(), sd[0].data_ptr(),
+                                      packed[1].data_ptr(), sd[1].data_ptr(), packed[2].data_ptr(),
+                                      sd[2].data_ptr(), group, sids, qd.data_ptr())
+    r.cache.sync_check()
+    eq, ek, ev = (O.f32_to_f16(O.w8a16_matmul(x, w, sc, group)).reshape(B, -1, D) for w, sc in ws)
+    if rope:
+        eq = np.stack([O.rope_row(eq[i], r.cos, r.sin, lens[i]) for i in range(B)])
+        ek = np.stack([O.rope_row(ek[i], r.cos, r.sin, lens[i]) for i in range(B)])
+    _close_f16_rows(from_dev(qd).reshape(B * Hq, D), eq.reshape(B * Hq, D), "Q")
+    base, n = r.cache.pool()
+    pool = d2h(base, n)
+    g = O.geom(L, Hkv, D, bs, r.cache.config.num_blocks, layout == T.TL_LAYOUT_HEAD_MAJOR)
+    for i, sid in enumerate(sids):
+        bt = np.array(r.cache.block_table(sid), np.int32)
+        k, v = O.gather(pool, g, bt, layer, lens[i] + 1)
+        _close_f16_rows(k[lens[i]], ek[i], f"K row of seq {sid}")
+        _close_f16_rows(v[lens[i]], ev[i], f"V row of seq {sid}")
+        assert r.cache.get_seq_len(sid) == lens[i]
+    r.check_pool_bit_exact()
+
+
+def test_project_qkv_append_packed_refuses_other_shapes():
+    """Group 16 (the mma.sync kernel's shape) has no packed form: the
+    packed entry refuses it before any launch."""
+    import torch
+    r = Run.create(L=1, Hq=8, Hkv=2, D=128, bs=16, max_seq_len=64, max_batch=2, rope=False)
+    sids = [r.allocate(64) for _ in range(2)]
+    buf = torch.zeros(1 << 20, dtype=torch.int8, device="cuda")
+    p = buf.data_ptr()
+    with pytest.raises(T.Unsupported) as e:
+        r.cache.project_qkv_append_packed(0, p, 256, p, p, p, p, p, p, 16, sids, p)
+    assert "packed weights need" in str(e.value)
+    r.cache.sync_check()

@@ -247,6 +247,45 @@ def test_project_qkv_append_validates_arguments():
     call(sids=[])  # nothing to do
 
 
+def test_project_qkv_append_packed_validates_arguments():
+    """tl_project_qkv_append_packed runs the same checks (under its own
+    name) before any device work, and tl_qkv_pack_weight refuses null,
+    misaligned and overlapping buffers and widths outside multiples of 128
+    before it looks for a device."""
+    c = make(2, 4, 64, 32, 2)
+    sid = c.allocate_sequence(2)
+
+    def call(layer=0, x=16, hidden=256, group=32, sids=(sid,)):
+        c.project_qkv_append_packed(layer, x, hidden, 16, 16, 16, 16, 16, 16, group, list(sids), 16)
+
+    with pytest.raises(T.InvalidArgument) as e:
+        call(layer=5)
+    assert "projectQKVAppendPacked" in str(e.value)
+    with pytest.raises(T.InvalidArgument):
+        call(x=None)
+    with pytest.raises(T.Unsupported):
+        call(hidden=200)
+    with pytest.raises(T.NotFound):
+        call(sids=(sid + 3,))
+    with pytest.raises(T.NoDevice):
+        call()
+    call(sids=())
+
+    with pytest.raises(T.InvalidArgument) as e:
+        T.pack_qkv_weight(None, 256, 128, 1 << 20)
+    assert "null" in str(e.value)
+    with pytest.raises(T.Unsupported):
+        T.pack_qkv_weight(1 << 20, 200, 128, 1 << 24)
+    with pytest.raises(T.Unsupported):
+        T.pack_qkv_weight(1 << 20, 256, 96, 1 << 24)
+    with pytest.raises(T.InvalidArgument) as e:
+        T.pack_qkv_weight((1 << 20) + 4, 256, 128, 1 << 24)
+    assert "aligned" in str(e.value)
+    with pytest.raises(T.InvalidArgument) as e:
+        T.pack_qkv_weight(1 << 20, 256, 128, (1 << 20) + 256 * 64)
+    assert "overlap" in str(e.value)
+
+
 def test_advance_clamps_to_capacity():  # :262-273
     c = make(2, 4, 8, 32, 2)
     sid = c.allocate_sequence(5)

@@ -167,7 +167,9 @@ constexpr int kMaxQkvRows = 64;
 struct QkvArgs {
     PoolGeom g;
     const void *x;           // fp16 [rows][K] activations
-    const int8_t *w[3];      // Q, K, V weights: int8 [K][n[i]] row-major
+    const int8_t *w[3];      // Q, K, V weights: int8 [K][n[i]] row-major, or
+                             // tile-blocked (qkv_pack_weight) when w_packed
+    int w_packed;            // tcgen05 kernel only
     const void *sc[3];       // fp16 scales [K / group][n[i]]
     int n[3];                // Hq*D, Hkv*D, Hkv*D
     int K, group, rows;
@@ -215,6 +217,12 @@ bool qkv_tc_supported(int head_dim, int group, int nq, int nkv, int hidden);
 int qkv_tc_rows_padded(int rows);
 bool qkv_tc_split(int hidden, int group, int rows, int tiles, int num_sms, int *ksplit, int *kchunk);
 cudaError_t launch_qkv_append_tc(const QkvArgs &a, cudaStream_t s);
+// Tile-blocked copy of one int8 weight [K][n] (K a multiple of 64, n of 128,
+// both pointers 16-byte aligned, not overlapping): column tile t, 64-row
+// block b is 8192 contiguous bytes at (t * K / 64 + b) * 8192, row r's
+// 16-byte chunk c at r * 128 + ((c ^ (r % 8)) * 16), the order in which a
+// 2-D TMA load with 128-byte swizzle leaves the same tile in shared memory.
+cudaError_t launch_qkv_pack_weight(const int8_t *w, int K, int n, int8_t *out, cudaStream_t s);
 
 
 }  // namespace tllm

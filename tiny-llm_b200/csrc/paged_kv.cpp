@@ -1055,10 +1055,10 @@ int tl_prefill_attention(tl_cache *c, int layer, const void *q, void *o, const i
 // and the appendKV of TransformerLayer::attention's decode step (reference
 // src/transformer.cpp:209-226, kernels/w8a16_matmul.cu:119-235,
 // src/kv_cache.cpp:206-233), batched over sequences.
-int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, const int8_t *wq, const void *sq,
-                          const int8_t *wk, const void *sk, const int8_t *wv, const void *sv, int group_size,
-                          const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream) {
-    static const char *ctx = "projectQKVAppend";
+static int project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, const int8_t *wq, const void *sq,
+                              const int8_t *wk, const void *sk, const int8_t *wv, const void *sv, int group_size,
+                              const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream, bool packed) {
+    const char *ctx = packed ? "projectQKVAppendPacked" : "projectQKVAppend";
     if (!c) return TL_ERR_INVALID_ARG;
     if (layer < 0 || layer >= c->cfg.num_layers)
         return set_error(c, TL_ERR_INVALID_ARG, layer_error(c, ctx, layer));
@@ -1118,6 +1118,11 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
               !mis(wk, 16) && !mis(wv, 16) && tc_plan(rows_max, &ks, &kchunk);
     int ks_last = 0, kchunk_last = 0;
     if (tc && rows_last > 0 && num_seqs > tllm::kMaxQkvRows) tc = tc_plan(rows_last, &ks_last, &kchunk_last);
+    if (packed && !tc)  // only the tcgen05 kernel reads the tile-blocked layout
+        return set_error(c, TL_ERR_UNSUPPORTED,
+                         std::string(ctx) + ": packed weights need Q, K and V widths in multiples of 128, "
+                                            "group_size 32/64/128, 16-byte aligned weights and a split of "
+                                            "hidden whose group accumulators fit TMEM");
     size_t need;
     if (tc) {
         // one fp32 accumulator per column tile
@@ -1184,6 +1189,7 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
         a.w[0] = wq;
         a.w[1] = wk;
         a.w[2] = wv;
+        a.w_packed = packed ? 1 : 0;
         a.sc[0] = sq;
         a.sc[1] = sk;
         a.sc[2] = sv;
@@ -1214,10 +1220,54 @@ int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, con
         }
         cudaError_t e = tc ? tllm::launch_qkv_append_tc(a, (cudaStream_t)stream)
                            : tllm::launch_qkv_append(a, (cudaStream_t)stream);
-        if (e != cudaSuccess) return cuda_fail(c, e, "projectQKVAppend: launch failed");
+        if (e != cudaSuccess)
+            return cuda_fail(c, e, packed ? "projectQKVAppendPacked: launch failed" : "projectQKVAppend: launch failed");
         ++c->launches;
     }
     for (Sequence *s : ss) s->written = std::max(s->written, s->len + 1);
+    return TL_OK;
+}
+
+int tl_project_qkv_append(tl_cache *c, int layer, const void *x, int hidden, const int8_t *wq, const void *sq,
+                          const int8_t *wk, const void *sk, const int8_t *wv, const void *sv, int group_size,
+                          const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream) {
+    return project_qkv_append(c, layer, x, hidden, wq, sq, wk, sk, wv, sv, group_size, seq_ids, num_seqs, q_out,
+                              stream, false);
+}
+
+// The same projections from weights repacked once by tl_qkv_pack_weight: each
+// CTA's weight blocks are then contiguous 8 KB copies instead of 64 row
+// segments of 128 bytes.
+int tl_project_qkv_append_packed(tl_cache *c, int layer, const void *x, int hidden, const int8_t *wq,
+                                 const void *sq, const int8_t *wk, const void *sk, const int8_t *wv, const void *sv,
+                                 int group_size, const int *seq_ids, int num_seqs, void *q_out, tl_stream_t stream) {
+    return project_qkv_append(c, layer, x, hidden, wq, sq, wk, sk, wv, sv, group_size, seq_ids, num_seqs, q_out,
+                              stream, true);
+}
+
+// Repacks one int8 weight [hidden][n] into the tile-blocked layout (once, at
+// model load). No handle: errors are read back with tl_last_error(NULL).
+int tl_qkv_pack_weight(const int8_t *w, int hidden, int n, int8_t *packed, tl_stream_t stream) {
+    auto fail = [](int st, const std::string &m) {
+        g_create_error = m;
+        return st;
+    };
+    if (!w || !packed) return fail(TL_ERR_INVALID_ARG, "packQKVWeight: a weight pointer is null");
+    if (hidden <= 0 || n <= 0 || hidden % 128 != 0 || n % 128 != 0)
+        return fail(TL_ERR_UNSUPPORTED, "packQKVWeight: hidden and n must be positive multiples of 128");
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(w), b0 = reinterpret_cast<uintptr_t>(packed);
+    if ((a0 & 15) || (b0 & 15)) return fail(TL_ERR_INVALID_ARG, "packQKVWeight: weights must be 16-byte aligned");
+    const uintptr_t bytes = (uintptr_t)hidden * (uintptr_t)n;
+    if (a0 < b0 + bytes && b0 < a0 + bytes)
+        return fail(TL_ERR_INVALID_ARG, "packQKVWeight: source and destination overlap");
+    int devices = 0;
+    if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) {
+        cudaGetLastError();
+        return fail(TL_ERR_NO_DEVICE, "packQKVWeight: no CUDA device");
+    }
+    cudaError_t e = tllm::launch_qkv_pack_weight(w, hidden, n, packed, (cudaStream_t)stream);
+    if (e != cudaSuccess)
+        return fail(TL_ERR_CUDA, std::string("packQKVWeight: launch failed: ") + cudaGetErrorString(e));
     return TL_OK;
 }
 

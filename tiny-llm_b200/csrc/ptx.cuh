@@ -206,6 +206,24 @@ __device__ __forceinline__ void tma_prefetch_2d(const void *tmap, int x, int y) 
                  : "memory");
 }
 
+// Contiguous bulk copy global -> shared (bytes a multiple of 16, both
+// addresses 16-byte aligned), completing on an mbarrier. No multicast: the
+// source is always this GPU's own memory.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+// Contiguous prefetch global -> L2 (bytes a multiple of 16, 16-byte aligned).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
+
 // A 16x16 tile of bytes (rows at the addresses of threads 0-15), transposed:
 // thread (g = lane / 4, t = lane % 4) receives r0 = bytes (4t..4t+3, g) and
 // r1 = bytes (4t..4t+3, g + 8) as (row, column) of the stored tile, the

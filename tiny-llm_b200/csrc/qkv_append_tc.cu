@@ -17,7 +17,10 @@
 //              (64 rows x 128 columns, 128-byte swizzle) and of its
 //              activation tile (64 K x N rows: the B layout) into a deep
 //              ring, completing on an mbarrier: the bytes in flight are the
-//              ring's, with no registers held;
+//              ring's, with no registers held. From weights repacked by
+//              qkv_pack_weight the tile is one contiguous 8 KB copy
+//              (cp.async.bulk) of bytes already in the swizzled order, where
+//              the row-major weights give 64 segments of 128 bytes;
 //   warps 0-7  convert each int8 tile to fp16 (exact: the byte in the
 //              mantissa of 1024.0, minus 1152) straight into TMEM, where the
 //              UMMA reads its A operand: a transposing ldmatrix of 16 x 16
@@ -180,6 +183,8 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
     const int klen = min(a.kchunk, a.K - k0);  // a multiple of 128 and of GS
     const int nblk = klen / kBlk;
     const int ngroups = klen / GS;
+    // tile-blocked weights: this CTA's blocks are nblk x 8 KB in a row
+    const int8_t *wpk = a.w[m] + ((long long)(col0 / kTcM) * (a.K / kBlk) + k0 / kBlk) * kW8Bytes;
     // TMEM: the group accumulators [kchunk / GS][NR columns], then the A ring
     const uint32_t acol0 = (uint32_t)(a.kchunk / GS * NR);
     const uint32_t tneed = acol0 + kNA * kACols;
@@ -190,9 +195,13 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
         // before this one on the stream may still run (programmatic launch):
         // a prefetch only warms L2, the loads themselves come after
         // griddepcontrol.wait like every other read.
-        ptx::prefetch_tensormap(&maps.w[m]);
         ptx::prefetch_tensormap(&maps.x);
-        for (int blk = 0; blk < nblk; ++blk) ptx::tma_prefetch_2d(&maps.w[m], col0, k0 + blk * kBlk);
+        if (a.w_packed) {
+            ptx::bulk_prefetch_l2(wpk, (uint32_t)(nblk * kW8Bytes));
+        } else {
+            ptx::prefetch_tensormap(&maps.w[m]);
+            for (int blk = 0; blk < nblk; ++blk) ptx::tma_prefetch_2d(&maps.w[m], col0, k0 + blk * kBlk);
+        }
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kNW; ++s) {
@@ -227,7 +236,10 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
                 }
                 const uint32_t dst = ptx::smem_u32(sw + s * Lay::kWStage);
                 ptx::mbar_arrive_expect_tx(loaded_u + 8 * s, (uint32_t)Lay::kWStage);
-                ptx::tma_load_2d(dst, maps.w[m], loaded_u + 8 * s, col0, k0 + blk * kBlk, stream);
+                if (a.w_packed)  // the same bytes, swizzled in memory: one contiguous copy
+                    ptx::bulk_load(dst, wpk + (long long)blk * kW8Bytes, (uint32_t)kW8Bytes, loaded_u + 8 * s, stream);
+                else
+                    ptx::tma_load_2d(dst, maps.w[m], loaded_u + 8 * s, col0, k0 + blk * kBlk, stream);
                 ptx::tma_load_2d(dst + kW8Bytes, maps.x, loaded_u + 8 * s, k0 + blk * kBlk, 0, keep);
             }
             ptx::griddep_launch_dependents();  // the next kernel may start prefetching its weights
@@ -512,7 +524,36 @@ cudaError_t launch_d(const QkvArgs &a, const QkvMaps &maps, cudaStream_t s) {
     }
 }
 
+// One thread per 16-byte chunk of the tile-blocked layout: packed row
+// (t * K / 64 + b) * 64 + r holds source row b * 64 + r, columns
+// t * 128 .. t * 128 + 127, its chunk c at position c ^ (r % 8).
+__global__ void qkv_pack_kernel(const int8_t *__restrict__ w, int K, int n, int8_t *__restrict__ out,
+                                long long chunks) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= chunks) return;
+    const int p = (int)(i & 7);
+    const long long prow = i >> 3;
+    const int r = (int)(prow & (kBlk - 1));
+    const long long tb = prow / kBlk;
+    const int kb = K / kBlk;
+    const long long t = tb / kb, b = tb % kb;
+    const int8_t *src = w + (b * kBlk + r) * (long long)n + t * kTcM + 16 * (p ^ (r & 7));
+    *reinterpret_cast<uint4 *>(out + 16 * i) = __ldg(reinterpret_cast<const uint4 *>(src));
+}
+
 }  // namespace
+
+cudaError_t launch_qkv_pack_weight(const int8_t *w, int K, int n, int8_t *out, cudaStream_t s) {
+    if (K <= 0 || n <= 0 || K % kBlk != 0 || n % kTcM != 0 || (reinterpret_cast<uintptr_t>(w) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15))
+        return cudaErrorInvalidValue;
+    const long long chunks = (long long)K * n / 16;
+    const int threads = 256;
+    const long long blocks = (chunks + threads - 1) / threads;
+    if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+    qkv_pack_kernel<<<(unsigned)blocks, threads, 0, s>>>(w, K, n, out, chunks);
+    return cudaGetLastError();
+}
 
 int qkv_tc_rows_padded(int rows) { return rows <= 16 ? 16 : (rows <= 32 ? 32 : 64); }
 
@@ -554,8 +595,8 @@ cudaError_t launch_qkv_append_tc(const QkvArgs &a, cudaStream_t s) {
     // tensor maps: each weight [K][n] int8 in 64-row x 128-column boxes; the
     // activations [rows][K] fp16 in 64 x (padded rows) boxes (rows past the
     // launch's read as zeros)
-    QkvMaps maps;
-    for (int i = 0; i < 3; ++i) {
+    QkvMaps maps = {};
+    for (int i = 0; i < 3 && !a.w_packed; ++i) {
         cudaError_t e = encode_tensor_map_2d(maps.w[i], false, a.w[i], (unsigned long long)a.n[i],
                                              (unsigned long long)a.K, (unsigned long long)a.n[i], kTcM, kBlk);
         if (e != cudaSuccess) return e;

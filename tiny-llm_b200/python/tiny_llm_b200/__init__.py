@@ -45,6 +45,7 @@ EXPORTED_SYMBOLS = [
     "tl_decode_attention_static", "tl_peer_init", "tl_peer_connect", "tl_peer_buffer",
     "tl_decode_attention_peer", "tl_attention_step", "tl_prefill_attention",
     "tl_project_qkv_append", "tl_sample_tokens", "tl_set_peer_wait_limit", "tl_debug_peer_attach",
+    "tl_qkv_pack_weight", "tl_project_qkv_append_packed",
 ]
 
 
@@ -144,6 +145,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
         "tl_attention_step": (i, [vp, i, vp, vp, vp, vp, ip, i, f, vp]),
         "tl_prefill_attention": (i, [vp, i, vp, vp, ip, ip, i, f, vp]),
         "tl_project_qkv_append": (i, [vp, i, vp, i, vp, vp, vp, vp, vp, vp, i, ip, i, vp, vp]),
+        "tl_project_qkv_append_packed": (i, [vp, i, vp, i, vp, vp, vp, vp, vp, vp, i, ip, i, vp, vp]),
+        "tl_qkv_pack_weight": (i, [vp, i, i, vp, vp]),
         "tl_sample_tokens": (i, [vp, ll, i, i, i, f, i, f, C.c_ulonglong, C.c_ulonglong, vp, vp]),
         "tl_sync_check": (i, [vp, vp]),
         "tl_rope_table": (None, [C.POINTER(C.c_float), C.POINTER(C.c_float), i, i, f]),
@@ -325,6 +328,13 @@ class KVCache:
                                                     sv, int(group_size), _ids(seq_ids), len(seq_ids), q_ptr,
                                                     stream or None))
 
+    def project_qkv_append_packed(self, layer, x_ptr, hidden, wq, sq, wk, sk, wv, sv, group_size, seq_ids,
+                                  q_ptr, stream=0):
+        """project_qkv_append with wq/wk/wv repacked by pack_qkv_weight."""
+        self._check(self._lib.tl_project_qkv_append_packed(self._h, int(layer), x_ptr, int(hidden), wq, sq, wk,
+                                                           sk, wv, sv, int(group_size), _ids(seq_ids),
+                                                           len(seq_ids), q_ptr, stream or None))
+
     # -- head-sharded peer gather (one process per GPU) ----------------------
     def peer_init(self, rank: int, world: int, gather_bytes: int) -> bytes:
         """Allocates this rank's gather region; returns its 64-byte IPC handle."""
@@ -395,6 +405,15 @@ def sample_tokens(logits_ptr, row_stride, rows, vocab, tokens_ptr, do_sample=Fal
     st = lib.tl_sample_tokens(logits_ptr, int(row_stride), int(rows), int(vocab), int(bool(do_sample)),
                               float(temperature), int(top_k), float(top_p), int(seed) & (2**64 - 1),
                               int(step) & (2**64 - 1), tokens_ptr, stream or None)
+    if st != TL_OK:
+        raise _ERRORS.get(st, TLError)(st, lib.tl_last_error(None).decode())
+
+
+def pack_qkv_weight(w_ptr, hidden, n, out_ptr, stream=0):
+    """tl_qkv_pack_weight: int8 [hidden][n] weights into the tile-blocked
+    layout project_qkv_append_packed reads (out: hidden * n bytes)."""
+    lib = load()
+    st = lib.tl_qkv_pack_weight(w_ptr, int(hidden), int(n), out_ptr, stream or None)
     if st != TL_OK:
         raise _ERRORS.get(st, TLError)(st, lib.tl_last_error(None).decode())
 
