@@ -137,6 +137,15 @@ class KVCacheManager {
                                   const int8_t *wk, const half *sk, const int8_t *wv, const half *sv,
                                   int group_size, const std::vector<int> &seq_ids, half *q_out,
                                   cudaStream_t stream = 0);
+    // The same from weights repacked once by packQKVWeight (tile-blocked,
+    // each 64-row block of a 128-column tile 8 KB contiguous).
+    Result<void> projectQKVAppendPacked(int layer_idx, const half *x, int hidden, const int8_t *wq,
+                                        const half *sq, const int8_t *wk, const half *sk, const int8_t *wv,
+                                        const half *sv, int group_size, const std::vector<int> &seq_ids,
+                                        half *q_out, cudaStream_t stream = 0);
+    // Repacks one int8 weight [hidden][n] into `packed` (hidden * n bytes of
+    // device memory) for projectQKVAppendPacked; asynchronous on `stream`.
+    static Result<void> packQKVWeight(const int8_t *w, int hidden, int n, int8_t *packed, cudaStream_t stream = 0);
     Result<std::vector<int>> getBlockTable(int seq_id) const;
     tl_pool_stats getPoolStats() const noexcept;
     Result<void> syncCheck(cudaStream_t stream = 0);

@@ -212,6 +212,12 @@ int main(int argc, char **argv) {
         EXPECT(has(call(0, H(256), 256, H(256), 32, {id, id}), "duplicate"));
         if (!g_gpu) EXPECT(has(call(0, H(256), 256, H(256), 32, {id}), "no CUDA device"));
         EXPECT(cache->getSeqLen(id) == 0);
+        // the packed entry: the same checks under its own name
+        auto packed = cache->projectQKVAppendPacked(0, H(256), 200, w, H(256), w, H(256), w, H(256), 32, {id}, q);
+        EXPECT(has(packed, "projectQKVAppendPacked") && has(packed, "supported shapes"));
+        EXPECT(has(KVCacheManager::packQKVWeight(nullptr, 256, 128, const_cast<int8_t *>(w)), "null"));
+        EXPECT(has(KVCacheManager::packQKVWeight(w, 256, 96, reinterpret_cast<int8_t *>(uintptr_t(1) << 24)),
+                   "multiples of 128"));
     });
     run("ResultMapAndFlatMap", [] {  // the reference's tests/test_cuda_utils.cpp:46,53 use them
         auto doubled = Result<int>::ok(21).map([](int x) { return 2 * x; });

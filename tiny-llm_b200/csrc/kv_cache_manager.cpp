@@ -121,6 +121,21 @@ Result<void> KVCacheManager::projectQKVAppend(int layer_idx, const half *x, int 
                                         seq_ids.data(), (int)seq_ids.size(), q_out, stream));
 }
 
+Result<void> KVCacheManager::projectQKVAppendPacked(int layer_idx, const half *x, int hidden, const int8_t *wq,
+                                                    const half *sq, const int8_t *wk, const half *sk,
+                                                    const int8_t *wv, const half *sv, int group_size,
+                                                    const std::vector<int> &seq_ids, half *q_out,
+                                                    cudaStream_t stream) {
+    return status(tl_project_qkv_append_packed(h_, layer_idx, x, hidden, wq, sq, wk, sk, wv, sv, group_size,
+                                               seq_ids.data(), (int)seq_ids.size(), q_out, stream));
+}
+
+Result<void> KVCacheManager::packQKVWeight(const int8_t *w, int hidden, int n, int8_t *packed,
+                                           cudaStream_t stream) {
+    if (tl_qkv_pack_weight(w, hidden, n, packed, stream) != TL_OK) return Result<void>::err(tl_last_error(nullptr));
+    return Result<void>::ok();
+}
+
 Result<std::vector<int>> KVCacheManager::getBlockTable(int seq_id) const {
     int n = 0;
     if (tl_get_block_table(h_, seq_id, nullptr, 0, &n) != TL_OK)
