@@ -26,7 +26,9 @@
 // exact integers: each weight exp((l - max) / T) <= 1 in units of 2^-40, so
 // histogram sums are associative and every CTA of the cluster derives the
 // same thresholds. Every warp fills its own histogram copy (no atomics
-// between warps), the CTA sums its copies, every CTA sums the cluster's CTA
+// between warps; a mass bin is two 32-bit words, the low word's atomic add
+// returning the carry into the high one, since 32-bit shared-memory atomics
+// are far cheaper than 64-bit ones), the CTA sums its copies, every CTA sums the cluster's CTA
 // histograms through distributed shared memory, and one warp turns the
 // result into suffix sums and finds thresholds with ballots. The index
 // among equal keys comes from per-CTA counts, a prefix over the cluster's
@@ -85,7 +87,8 @@ struct Pub {
 };
 
 struct Shared {
-    u64 wmass[kWarps][256];  // per-warp histograms
+    unsigned wlo[kWarps][256];  // per-warp mass histograms: low and high words
+    unsigned whi[kWarps][256];
     unsigned wcnt[kWarps][256];
     u64 gmass[256];          // the cluster's histograms of the last pass
     unsigned gcnt[256];
@@ -229,7 +232,8 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
     // sel (sel < 0: every key), at their high byte (sel < 0) or low byte.
     auto histogram = [&](int sel) {
         for (int b = lane; b < 256; b += 32) {
-            sh.wmass[warp][b] = 0ull;
+            sh.wlo[warp][b] = 0u;
+            sh.whi[warp][b] = 0u;
             sh.wcnt[warp][b] = 0u;
         }
         __syncwarp();
@@ -237,7 +241,15 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
             const uint32_t key = skey[i];
             if (sel < 0 || (int)(key >> 8) == sel) {
                 const int b = sel < 0 ? (int)(key >> 8) : (int)(key & 0xFFu);
-                atomicAdd(&sh.wmass[warp][b], fx(key));
+                // the 64-bit mass as two 32-bit words: the low word's add
+                // returns the old value, whose wrap is the carry into the
+                // high word (added only when nonzero: masses of 2^32 units
+                // and more are the keys near the maximum)
+                const u64 x = fx(key);
+                const unsigned xlo = (unsigned)x;
+                const unsigned old = atomicAdd(&sh.wlo[warp][b], xlo);
+                const unsigned up = (unsigned)(x >> 32) + (old + xlo < old ? 1u : 0u);
+                if (up) atomicAdd(&sh.whi[warp][b], up);
                 atomicAdd(&sh.wcnt[warp][b], 1u);
             }
         }
@@ -247,7 +259,7 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
             u64 ms = 0ull;
             unsigned cs = 0u;
             for (int w = 0; w < kWarps; ++w) {
-                ms += sh.wmass[w][b];
+                ms += ((u64)sh.whi[w][b] << 32) + sh.wlo[w][b];
                 cs += sh.wcnt[w][b];
             }
             p.mass[b] = ms;
