@@ -27,8 +27,8 @@
 //              bytes hands every thread the bytes that tcgen05.st.16x256b
 //              stores as fp16 pairs along K, so shared memory carries the
 //              weights once (TMA in, ldmatrix out) and no fp16 copy of them;
-//              afterwards warps 0-3 read the accumulators (one TMEM lane =
-//              one weight column per thread);
+//              afterwards they read the accumulators (one TMEM lane = one
+//              weight column per thread; warps w and w + 4 split the rows);
 //   warp 8     issues the UMMAs (one thread) and owns the TMEM allocation.
 // Each scale group is summed by the tensor core into its own fp32 TMEM
 // accumulator (fresh at the group's first k-step); the epilogue scales the
@@ -325,8 +325,9 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
 
     __syncwarp();  // the MMA and producer warps' lane 0 rejoins its warp
 
-    // ---- epilogue: warps 0-3 read the group accumulators (thread = weight
-    // column; 16 rows at a time, three groups' TMEM loads per wait) and sum
+    // ---- epilogue: the converter warps read the group accumulators (thread
+    // = weight column; 16 rows at a time, three groups' TMEM loads per wait,
+    // warps w and w + 4 on alternate 16-row chunks) and sum
     // s_g * acc_g in group order into an fp32 [NR][128] tile in the TMA ring
     // (free: every load landed and every MMA completed) ----
     float *sf = reinterpret_cast<float *>(sw);
@@ -336,16 +337,19 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
     if (warp < kConvWarps) {
         ptx::named_barrier_sync(1, kConvThreads);  // every thread's scales landed
         const int nq4 = a.rows * (kTcM / 4);       // float4 chunks of the real rows
-        if (warp < 4) {
-            const int col = 32 * warp + lane;
+        {
+            // warps w and w + 4 share TMEM lane quarter w % 4 (weight columns)
+            // and take alternate 16-row chunks of it
+            constexpr int RC = 16, GB = 3;
+            const int q = warp & 3, rc0 = (warp >> 2) * RC;
+            const int col = 32 * q + lane;
             bool done_ok = ptx::mbar_wait_bounded(done_u, 0u, kWaitNs);
             if (!done_ok && lane == 0) atomicOr(g.err, kErrWaitTimeout);
             done_ok = __all_sync(0xffffffffu, done_ok) && ok;
             ptx::tc_fence_after_sync();
-            constexpr int RC = 16, GB = 3;
-            const uint32_t tl = tbase + ((uint32_t)(32 * warp) << 16);
+            const uint32_t tl = tbase + ((uint32_t)(32 * q) << 16);
 #pragma unroll
-            for (int rc = 0; rc < NR; rc += RC) {
+            for (int rc = rc0; rc < NR; rc += 2 * RC) {
                 float acc[RC];
 #pragma unroll
                 for (int r = 0; r < RC; ++r) acc[r] = 0.f;
