@@ -82,6 +82,13 @@ struct alignas(64) QkvMaps {
     unsigned char x[128];
 };
 
+// Scale groups one K-chunk of kchunk rows (a multiple of kBlk, starting at a
+// multiple of kchunk) can touch: a chunk that is not a multiple of the group
+// may start and end inside one.
+__host__ __device__ constexpr int tc_max_groups(int kchunk, int group) {
+    return kchunk % group == 0 ? kchunk / group : (kchunk - 1 + group - kBlk) / group + 1;
+}
+
 __device__ __forceinline__ uint32_t swz(int row, int chunk) { return row * 128 + (((chunk & 7) ^ (row & 7)) << 4); }
 
 __device__ __forceinline__ long long pool_off(const PoolGeom &g, int layer, int kv, int block, int tok, int head) {
@@ -163,8 +170,9 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sw = smem;                                     // TMA ring [kNW][int8 weights | activations]
-    __half *ssc = reinterpret_cast<__half *>(smem + Lay::kRing);  // the chunk's scales [kchunk / GS][128]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Lay::kRing + (a.kchunk / GS) * kTcM * 2);
+    const int maxg = tc_max_groups(a.kchunk, GS);
+    __half *ssc = reinterpret_cast<__half *>(smem + Lay::kRing);  // the chunk's scales [groups][128]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Lay::kRing + maxg * kTcM * 2);
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 24);
     const uint32_t loaded_u = ptx::smem_u32(bars);          // [kNW] TMA stage landed
     const uint32_t wfree_u = loaded_u + 8 * kNW;            // [kNW] TMA stage consumed (MMAs done)
@@ -180,13 +188,14 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
     const int col0 = kTcM * (tile - (m == 0 ? 0 : (m == 1 ? tq : tq + tk)));
     const int N = a.n[m];
     const int k0 = kc * a.kchunk;
-    const int klen = min(a.kchunk, a.K - k0);  // a multiple of 128 and of GS
+    const int klen = min(a.kchunk, a.K - k0);  // a multiple of kBlk
     const int nblk = klen / kBlk;
-    const int ngroups = klen / GS;
+    const int gfirst = k0 / GS;                          // the chunk's first scale group
+    const int ngroups = (k0 + klen - 1) / GS - gfirst + 1;  // the first and last may be partial
     // tile-blocked weights: this CTA's blocks are nblk x 8 KB in a row
     const int8_t *wpk = a.w[m] + ((long long)(col0 / kTcM) * (a.K / kBlk) + k0 / kBlk) * kW8Bytes;
-    // TMEM: the group accumulators [kchunk / GS][NR columns], then the A ring
-    const uint32_t acol0 = (uint32_t)(a.kchunk / GS * NR);
+    // TMEM: the group accumulators [maxg][NR columns], then the A ring
+    const uint32_t acol0 = (uint32_t)(maxg * NR);
     const uint32_t tneed = acol0 + kNA * kACols;
     const uint32_t tcols = tneed <= 32 ? 32u : tneed <= 64 ? 64u : tneed <= 128 ? 128u : tneed <= 256 ? 256u : 512u;
 
@@ -248,7 +257,7 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
         // ---- converters: the chunk's scales (cp.async), then int8 -> fp16 ----
         const int t = threadIdx.x;
         {
-            const __half *S = static_cast<const __half *>(a.sc[m]) + (long long)(k0 / GS) * N + col0;
+            const __half *S = static_cast<const __half *>(a.sc[m]) + (long long)gfirst * N + col0;
             const uint32_t ssc_u = ptx::smem_u32(ssc);
             for (int i = t; i < ngroups * (kTcM / 8); i += kConvThreads) {
                 const int gi = i / (kTcM / 8), c8 = i % (kTcM / 8);
@@ -311,10 +320,11 @@ __global__ void __launch_bounds__(kThreadsTc, NR <= 32 ? 2 : 1) qkv_append_tc_ke
 #pragma unroll
             for (int ks = 0; ks < kBlk / 16; ++ks) {
                 const int kk = blk * (kBlk / 16) + ks;  // k-step within the chunk
-                const int grp = kk * 16 / GS;
+                const int ka = k0 + kk * 16;  // the k-step's first row
+                const int grp = ka / GS - gfirst;
                 const uint32_t at = tbase + acol0 + (uint32_t)(sa_i * kACols + 8 * ks);
                 const uint64_t bd = ptx::umma_desc_sw128(xa + ks * 32, 16, 1024);
-                ptx::umma_f16_ta(tbase + (uint32_t)(grp * NR), at, bd, idesc, (kk * 16) % GS ? 1u : 0u);
+                ptx::umma_f16_ta(tbase + (uint32_t)(grp * NR), at, bd, idesc, (ka % GS && kk) ? 1u : 0u);
             }
             ptx::umma_commit(afree_u + 8 * sa_i);
             ptx::umma_commit(wfree_u + 8 * s);
@@ -570,30 +580,34 @@ bool qkv_tc_supported(int head_dim, int group, int nq, int nkv, int hidden) {
 // rows, one CTA per SM at 64.
 static int tc_tmem_budget(int nr) { return nr <= 32 ? 256 : 512; }
 
-// K-chunk (a multiple of 128 rows) and split for a launch of `rows` rows:
+// K-chunk (a multiple of 64 rows) and split for a launch of `rows` rows:
 // about one wave of CTAs (two per SM up to 32 rows, one at 64), at most
 // kMaxSplit CTAs per tile, each chunk's group accumulators plus the A ring
-// within the CTA's TMEM columns.
+// within the CTA's TMEM columns. Chunks need not hold whole scale groups, so
+// 64 blocks of 64 rows split six ways are chunks of 11 blocks (the longest
+// CTA streams 11 blocks, not the 12 of 128-row units).
 bool qkv_tc_split(int hidden, int group, int rows, int tiles, int num_sms, int *ksplit, int *kchunk) {
     const int nr = qkv_tc_rows_padded(rows);
-    const int units = hidden / 128;
-    const int per_unit = 128 / group * nr;  // accumulator columns per 128 rows of K
-    const int cap = (tc_tmem_budget(nr) - kNA * kACols) / per_unit;
-    if (units < 1 || cap < 1) return false;
+    const int blocks = hidden / kBlk;
+    const int budget = tc_tmem_budget(nr) - kNA * kACols;  // accumulator columns
+    if (blocks < 1) return false;
     const int per_sm = nr <= 32 ? 2 : 1;
     int ks = std::max(1, (per_sm * std::max(num_sms, 1)) / std::max(tiles, 1));
-    ks = std::min({ks, units, kMaxSplit});
-    const int per = std::min((units + ks - 1) / ks, cap);
-    if ((units + per - 1) / per > kMaxSplit) return false;
-    *kchunk = per * 128;
-    *ksplit = (units + per - 1) / per;
+    ks = std::min({ks, blocks, kMaxSplit});
+    int per = (blocks + ks - 1) / ks;  // blocks per chunk
+    while (per > 0 && tc_max_groups(per * kBlk, group) * nr > budget) --per;
+    if (per < 1 || (blocks + per - 1) / per > kMaxSplit) return false;
+    *kchunk = per * kBlk;
+    *ksplit = (blocks + per - 1) / per;
     return true;
 }
 
 cudaError_t launch_qkv_append_tc(const QkvArgs &a, cudaStream_t s) {
     if (a.rows <= 0) return cudaSuccess;
-    if (a.rows > kMaxQkvRows || a.kchunk % 128 != 0 || a.ksplit < 1 || a.ksplit > kMaxSplit ||
-        (long long)a.kchunk / a.group * qkv_tc_rows_padded(a.rows) + kNA * kACols >
+    if (a.rows > kMaxQkvRows || a.kchunk <= 0 || a.kchunk % kBlk != 0 || a.ksplit < 1 || a.ksplit > kMaxSplit ||
+        (long long)(a.ksplit - 1) * a.kchunk >= a.K || (long long)a.ksplit * a.kchunk < a.K ||
+        (a.group != 32 && a.group != 64 && a.group != 128) ||
+        tc_max_groups(a.kchunk, a.group) * qkv_tc_rows_padded(a.rows) + kNA * kACols >
             tc_tmem_budget(qkv_tc_rows_padded(a.rows)))
         return cudaErrorInvalidValue;
     // tensor maps: each weight [K][n] int8 in 64-row x 128-column boxes; the
