@@ -30,7 +30,11 @@
 // returning the carry into the high one, since 32-bit shared-memory atomics
 // are far cheaper than 64-bit ones), the CTA sums its copies, every CTA sums the cluster's CTA
 // histograms through distributed shared memory, and one warp turns the
-// result into suffix sums and finds thresholds with ballots. The index
+// result into suffix sums and finds thresholds with ballots. Once the first
+// pass has placed the threshold in a high-byte bin, every CTA lists the slice
+// positions of its keys in that bin and above (up to 4096; more, and the
+// later passes scan the whole slice as before), and the later passes (low
+// bytes of one such bin, the drawn key's count) read only the list. The index
 // among equal keys comes from per-CTA counts, a prefix over the cluster's
 // ranks (slices are in index order) and one block-wide scan in the CTA that
 // holds it.
@@ -52,6 +56,7 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxSlice = 65536;  // keys per CTA: vocabularies up to kCtas * kMaxSlice
 constexpr float kFx = 1099511627776.0f;  // 2^40: the unit of an integer mass
+constexpr int kCandCap = 4096;    // slice positions of the keys at or above the threshold bin
 
 using u64 = unsigned long long;
 
@@ -102,6 +107,8 @@ struct Shared {
     unsigned wpre[kWarps];
     u64 s_u[4];
     int s_int[4];
+    unsigned ncand;
+    uint16_t cand[kCandCap];  // the candidates' slice positions (any order)
 };
 
 __device__ __forceinline__ u64 warp_max64(u64 v) {
@@ -227,6 +234,8 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
         return key == 0u ? 0ull : (u64)__float2ull_rn(exp2f((value_of(key) - m) * c) * kFx);
     };
 
+    bool use_list = false;  // set once the candidates are listed (after the first pass)
+    int ncand = 0;
     // One histogram pass over the slice and its cluster reduction into
     // sh.gmass / sh.gcnt and their suffix sums: the keys with high byte ==
     // sel (sel < 0: every key), at their high byte (sel < 0) or low byte.
@@ -237,7 +246,12 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
             sh.wcnt[warp][b] = 0u;
         }
         __syncwarp();
-        for (int i = tid; i < n; i += kThreads) {
+        // a later pass looks at one bin at or above the threshold bin: the
+        // candidate list holds all of its keys when it did not overflow
+        const bool from_list = sel >= 0 && use_list;
+        const int cnt_keys = from_list ? ncand : n;
+        for (int c = tid; c < cnt_keys; c += kThreads) {
+            const int i = from_list ? (int)sh.cand[c] : c;
             const uint32_t key = skey[i];
             if (sel < 0 || (int)(key >> 8) == sel) {
                 const int b = sel < 0 ? (int)(key >> 8) : (int)(key & 0xFFu);
@@ -319,7 +333,26 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
     const unsigned c_above1 = (unsigned)sh.s_int[1];
     const u64 p_target = sh.s_u[0];
     const u64 m_above1 = sh.amass1[bh];
+    // ---- list the slice positions of the keys in bin bh and above: every
+    // later pass (the low bytes of a bin >= bh, the drawn key's count) reads
+    // only them. One warp-aggregated shared-memory atomic per warp and round;
+    // past kCandCap entries the passes scan the whole slice instead.
+    if (tid == 0) sh.ncand = 0u;
     __syncthreads();
+    for (int base = 0; base < n; base += kThreads) {
+        const int i = base + tid;
+        const bool take = i < n && (int)(skey[i] >> 8) >= bh;
+        const unsigned mask = __ballot_sync(0xffffffffu, take);
+        if (mask) {
+            unsigned pos = 0u;
+            if (lane == 0) pos = atomicAdd(&sh.ncand, (unsigned)__popc(mask));
+            pos = __shfl_sync(0xffffffffu, pos, 0) + (unsigned)__popc(mask & ((1u << lane) - 1u));
+            if (take && pos < (unsigned)kCandCap) sh.cand[pos] = (uint16_t)i;
+        }
+    }
+    __syncthreads();
+    ncand = (int)sh.ncand;
+    use_list = ncand <= kCandCap;
 
     histogram(bh);  // the low bytes of bin bh
     if (warp == 0) {
@@ -398,8 +431,12 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
     // over the ranks, then a block-wide scan in the CTA that holds it
     const int chunk = (n + kThreads - 1) / kThreads;
     const int i0 = min(n, tid * chunk), i1 = min(n, i0 + chunk);
-    unsigned cnt = 0;
-    for (int i = i0; i < i1; ++i) cnt += skey[i] == ks;
+    unsigned cnt = 0;  // this thread's contiguous range (the scan below); the list when it serves
+    if (use_list) {
+        for (int c = tid; c < ncand; c += kThreads) cnt += skey[sh.cand[c]] == ks;
+    } else {
+        for (int i = i0; i < i1; ++i) cnt += skey[i] == ks;
+    }
     const unsigned wcount = warp_sum(cnt);
     if (lane == 0) sh.redu[warp] = wcount;
     __syncthreads();
@@ -426,6 +463,10 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
     const int jl = sh.s_int[0];
     if (sh.s_int[1] == 0 && rank == 0 && tid == 0) a.tokens[row] = argmax;  // (cannot happen)
     if (sh.s_int[2]) {  // this CTA holds the drawn index
+        if (use_list) {  // the list is in no particular order: count the contiguous ranges
+            cnt = 0;
+            for (int i = i0; i < i1; ++i) cnt += skey[i] == ks;
+        }
         unsigned incl = cnt;  // inclusive scan over the block: warp shuffles, then warp totals
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
