@@ -458,6 +458,59 @@ def test_project_qkv_append_llama3_shape(packed):
     r.check_pool_bit_exact()
 
 
+@pytest.mark.parametrize("D,G,B,hidden,group,rope,packed", [
+    (128, 4, 20, 1152, 128, True, False),   # chunks of 3 blocks: scale groups split between CTAs
+    (64, 8, 16, 384, 64, True, True),       # six CTAs of one block each
+    (128, 2, 32, 640, 128, False, True),    # five CTAs of two blocks
+    (128, 4, 1, 4096, 128, True, False),    # one row
+])
+def test_project_qkv_append_split_shapes(D, G, B, hidden, group, rope, packed):
+    """K-splits whose chunks split scale groups between CTAs, one-block
+    chunks, an uneven last chunk and a single row: Q and every K/V row
+    within two fp16 units of the oracle, and the rest of the pool
+    untouched."""
+    import torch
+    Hkv = 2
+    Hq = Hkv * G
+    r = Run.create(L=2, Hq=Hq, Hkv=Hkv, D=D, bs=16, max_seq_len=96, max_batch=B, rope=rope,
+                   layout=T.TL_LAYOUT_TOKEN_MAJOR, permute_seed=4)
+    lens = [(13 * i + 1) % 70 for i in range(B)]
+    sids = [r.allocate(96) for _ in range(B)]
+    for i, (sid, P) in enumerate(zip(sids, lens)):
+        if P:
+            r.prefill(sid, P, seed=900 + i)
+    x = O.normal_f16((B, hidden), 321 + B)
+    ws = [_qkv_weights(hidden, nc, group, 51 + j) for j, nc in enumerate((Hq * D, Hkv * D, Hkv * D))]
+    xd = to_dev(x)
+    wd = [torch.from_numpy(w.copy()).cuda() for w, _ in ws]
+    sd = [to_dev(sc) for _, sc in ws]
+    if packed:
+        pk = [torch.empty_like(w) for w in wd]
+        for w, p in zip(wd, pk):
+            T.pack_qkv_weight(w.data_ptr(), hidden, w.shape[1], p.data_ptr())
+        wd = pk
+    layer = 1
+    qd = torch.full((B, Hq * D), 0x7e00, dtype=torch.int16, device="cuda")
+    proj = r.cache.project_qkv_append_packed if packed else r.cache.project_qkv_append
+    proj(layer, xd.data_ptr(), hidden, wd[0].data_ptr(), sd[0].data_ptr(), wd[1].data_ptr(), sd[1].data_ptr(),
+         wd[2].data_ptr(), sd[2].data_ptr(), group, sids, qd.data_ptr())
+    r.cache.sync_check()
+    eq, ek, ev = (O.f32_to_f16(O.w8a16_matmul(x, w, sc, group)).reshape(B, -1, D) for w, sc in ws)
+    if rope:
+        eq = np.stack([O.rope_row(eq[i], r.cos, r.sin, lens[i]) for i in range(B)])
+        ek = np.stack([O.rope_row(ek[i], r.cos, r.sin, lens[i]) for i in range(B)])
+    _close_f16_rows(from_dev(qd).reshape(B * Hq, D), eq.reshape(B * Hq, D), "Q")
+    base, n = r.cache.pool()
+    pool = d2h(base, n)
+    g = O.geom(2, Hkv, D, 16, r.cache.config.num_blocks, False)
+    for i, sid in enumerate(sids):
+        bt = np.array(r.cache.block_table(sid), np.int32)
+        k, v = O.gather(pool, g, bt, layer, lens[i] + 1)
+        _close_f16_rows(k[lens[i]], ek[i], f"K row of seq {sid}")
+        _close_f16_rows(v[lens[i]], ev[i], f"V row of seq {sid}")
+    r.check_pool_bit_exact()
+
+
 def test_project_qkv_append_packed_refuses_other_shapes():
     """Group 16 (the mma.sync kernel's shape) has no packed form: the
     packed entry refuses it before any launch."""
