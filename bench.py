@@ -62,6 +62,10 @@ CONFIGS = {
                rope=True, permute=True),
     "c4": dict(workload="c4 70B long-context GQA, 8 seqs @ ctx 32768 (1 GPU batch shard)",
                L=80, Hq=64, Hkv=8, D=128, bs=32, lens=[32768] * 8, rope=True),
+    # one rank's share of c2 with the batch split over 8 GPUs (4 sequences):
+    # the per-rank work of that strong-scaling point, on one GPU
+    "c2r8": dict(workload="c2 per-rank share at 8 GPUs (4 seqs @ ctx 2048)", L=32, Hq=32, Hkv=32,
+                 D=128, bs=16, lens=[2048] * 4, rope=True),
     # one rank's slice of c4 head-sharded over 8 GPUs (1 KV head, its 8 query
     # heads, all 8 sequences): the local work of that mode, on one GPU
     "c4r8": dict(workload="c4 per-rank slice of the 8-way head shard (1 KV head, 8 q heads)",

@@ -168,8 +168,12 @@ extern "C" int tl_decode_attention_static(const tl_paged_view *view, int layer, 
                                 "0..num_rows-1"));
         a.slot[i] = table_rows[i];
         a.len[i] = S;
-        a.prefix[i + 1] = a.prefix[i] + tllm::unit_slots((S + tllm::kDecodeTile - 1) / tllm::kDecodeTile);
     }
+    long long real_tiles = 0;  // the per-unit overhead charge follows the tiles per worker
+    for (int i = 0; i < num_seqs; ++i) real_tiles += (seq_lens[i] + tllm::kDecodeTile - 1) / tllm::kDecodeTile;
+    a.vslots = tllm::unit_overhead_slots((long long)Hkv * real_tiles, std::min<long long>(max_workers, cap_workers));
+    for (int i = 0; i < num_seqs; ++i)
+        a.prefix[i + 1] = a.prefix[i] + tllm::unit_slots((seq_lens[i] + tllm::kDecodeTile - 1) / tllm::kDecodeTile, a.vslots);
     if (!v.error_word) {
         e = cudaMemsetAsync(scratch, 0, sizeof(int), stream);
         if (e != cudaSuccess)

@@ -28,9 +28,16 @@ constexpr int kDecodeTile = 16;
 constexpr int kInKernelMergeMaxPieces = 12;
 // Work slots charged to each (sequence, kv_head) unit on top of its tiles:
 // the unit's fixed cost (Q load, finalize, output) in tile-equivalents, so
-// that the stream-K split balances time, not just tiles.
+// that the stream-K split balances time, not just tiles. A call with few
+// tiles per worker (a batch split over many GPUs) charges more: there the
+// fixed cost is a larger share of each worker's time.
 constexpr int kUnitOverheadSlots = 2;
-inline int unit_slots(int tiles) { return tiles > 0 ? tiles + kUnitOverheadSlots : 0; }
+constexpr int kUnitOverheadSlotsFew = 4;
+constexpr int kFewTilesPerWorker = 48;
+inline int unit_overhead_slots(long long tiles, long long workers) {
+    return tiles < kFewTilesPerWorker * workers ? kUnitOverheadSlotsFew : kUnitOverheadSlots;
+}
+inline int unit_slots(int tiles, int vslots) { return tiles > 0 ? tiles + vslots : 0; }
 
 // Pool geometry shared by every kernel.
 struct PoolGeom {
@@ -116,6 +123,7 @@ struct DecodeArgs {
     int nseq;
     long long total_items;  // W
     int workers;            // V
+    int vslots;             // virtual slots per unit (unit_overhead_slots)
     int slot[kMaxDecodeSeqs];     // block-table row of each sequence
     int len[kMaxDecodeSeqs];      // attended tokens of each sequence
     int prefix[kMaxDecodeSeqs + 1];  // prefix sums of unit_slots(tiles) per sequence

@@ -73,16 +73,16 @@ constexpr int kPartialRow = D + 4;
 
 // Position of a work slot. The work of a call is a list of slots in
 // sequence-major, then kv-head order; unit (b, kvh) owns us =
-// unit_slots(tiles of b) consecutive slots: kUnitOverheadSlots virtual slots
+// unit_slots(tiles of b) consecutive slots: vs = a.vslots virtual slots
 // (no data: they stand for the unit's fixed cost — Q load, finalize — so
 // that equal slot ranges mean equal time) followed by its real 16-token
-// tiles. tile = slot - kUnitOverheadSlots (< 0: virtual).
+// tiles. tile = slot - vs (< 0: virtual).
 struct ItemPos {
-    int b, kvh, slot, us;
+    int b, kvh, slot, us, vs;
     long long unit_first;  // first slot of the unit (its virtual slots)
-    __device__ __forceinline__ int tile() const { return slot - kUnitOverheadSlots; }
-    __device__ __forceinline__ int nb() const { return us - kUnitOverheadSlots; }
-    __device__ __forceinline__ long long real_first() const { return unit_first + kUnitOverheadSlots; }
+    __device__ __forceinline__ int tile() const { return slot - vs; }
+    __device__ __forceinline__ int nb() const { return us - vs; }
+    __device__ __forceinline__ long long real_first() const { return unit_first + vs; }
     __device__ __forceinline__ long long last() const { return unit_first + us - 1; }
 };
 
@@ -259,6 +259,7 @@ __device__ __forceinline__ ItemPos locate(const DecodeArgs &a, long long w) {
         else hi = mid - 1;
     }
     ItemPos p;
+    p.vs = a.vslots;
     p.b = lo;
     p.us = a.prefix[lo + 1] - a.prefix[lo];
     const int r = (int)(w - (long long)H * a.prefix[lo]);  // < H * us < 2^31
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
             lt0 += __shfl_xor_sync(0xffffffffu, lt0, off);
             lt1 += __shfl_xor_sync(0xffffffffu, lt1, off);
         }
-        const bool complete = ufirst + kUnitOverheadSlots >= ws && ufirst + uus <= we;
+        const bool complete = ufirst + a.vslots >= ws && ufirst + uus <= we;
         const int g0 = 2 * tig, g1 = 2 * tig + 1;
         if (complete) {
             // stage the unit's [G][D] fp16 output in shared memory, then
@@ -577,7 +578,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
                 // an atomic ticket, no waiting on other workers.
                 __threadfence();
                 __syncwarp();
-                const long long v_first = worker_of_item(ufirst + kUnitOverheadSlots, W, V);
+                const long long v_first = worker_of_item(ufirst + a.vslots, W, V);
                 const long long v_last = worker_of_item(ufirst + uus - 1, W, V);
                 int *ctr = a.counters + ((long long)ub * H + ukvh);
                 int last = 0;
@@ -595,9 +596,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 
     ItemPos p = locate(a, ws);
     long long w = ws;  // current slot; virtual slots are jumped over
-    if (p.slot < kUnitOverheadSlots) {
-        w += kUnitOverheadSlots - p.slot;
-        p.slot = kUnitOverheadSlots;
+    if (p.slot < p.vs) {
+        w += p.vs - p.slot;
+        p.slot = p.vs;
     }
     int fail_at = -1;
     int k = 0;  // real tiles consumed; stage = k % kNS
@@ -611,8 +612,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
                     p.us = a.prefix[p.b + 1] - a.prefix[p.b];
                 } while (p.us == 0);
             }
-            p.slot = kUnitOverheadSlots;
-            w += kUnitOverheadSlots;
+            p.slot = p.vs;
+            w += p.vs;
             if (w >= we) break;
         }
         if (p.b != ub || p.kvh != ukvh) {
@@ -783,7 +784,7 @@ __device__ __forceinline__ void merge_body(const DecodeArgs &a) {
     if (us == 0) return;
     const long long W = a.total_items, V = a.workers;
     const long long unit_first = (long long)H * a.prefix[b] + (long long)kvh * us;
-    const long long v_first = worker_of_item(unit_first + kUnitOverheadSlots, W, V);
+    const long long v_first = worker_of_item(unit_first + a.vslots, W, V);
     const long long v_last = worker_of_item(unit_first + us - 1, W, V);
     if (v_first == v_last) return;
     const int c = threadIdx.x % kChunks, sg = threadIdx.x / kChunks;

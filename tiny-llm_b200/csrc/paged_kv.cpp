@@ -869,12 +869,15 @@ int decode_impl(tl_cache *c, const char *ctx, int layer, const void *q, void *o,
             a.slice_bytes = slice;
             a.peer_wait_ns = c->peer_wait_ns;
         }
+        long long real_tiles = 0;  // the per-unit overhead charge follows the tiles per worker
+        for (int i = 0; i < n; ++i) real_tiles += ceil_div(ss[(size_t)(j0 + i)]->written, tllm::kDecodeTile);
+        a.vslots = tllm::unit_overhead_slots((long long)Hkv * real_tiles, c->max_workers);
         a.prefix[0] = 0;
         for (int i = 0; i < n; ++i) {
             const Sequence *s = ss[(size_t)(j0 + i)];
             a.slot[i] = s->slot;
             a.len[i] = s->written;
-            a.prefix[i + 1] = a.prefix[i] + tllm::unit_slots(ceil_div(s->written, tllm::kDecodeTile));
+            a.prefix[i + 1] = a.prefix[i] + tllm::unit_slots(ceil_div(s->written, tllm::kDecodeTile), a.vslots);
             if (s->written == 0) {  // nothing to attend: zeros, as documented
                 const int ndst = peer ? a.ndst : 1;
                 for (int r = 0; r < ndst; ++r) {
