@@ -66,6 +66,13 @@ CONFIGS = {
     # the per-rank work of that strong-scaling point, on one GPU
     "c2r8": dict(workload="c2 per-rank share at 8 GPUs (4 seqs @ ctx 2048)", L=32, Hq=32, Hkv=32,
                  D=128, bs=16, lens=[2048] * 4, rope=True),
+    "c2r2": dict(workload="c2 per-rank share at 2 GPUs (16 seqs @ ctx 2048)", L=32, Hq=32, Hkv=32,
+                 D=128, bs=16, lens=[2048] * 16, rope=True),
+    "c3r2": dict(workload="c3-shaped per-rank share at 2 GPUs (32 ragged seqs ctx U[512,8192])",
+                 L=32, Hq=32, Hkv=8, D=128, bs=16, lens="ragged", B=32, lo=512, hi=8192,
+                 rope=True, permute=True),
+    "c2r4": dict(workload="c2 per-rank share at 4 GPUs (8 seqs @ ctx 2048)", L=32, Hq=32, Hkv=32,
+                 D=128, bs=16, lens=[2048] * 8, rope=True),
     # one rank's slice of c4 head-sharded over 8 GPUs (1 KV head, its 8 query
     # heads, all 8 sequences): the local work of that mode, on one GPU
     "c4r8": dict(workload="c4 per-rank slice of the 8-way head shard (1 KV head, 8 q heads)",

@@ -33,7 +33,7 @@ constexpr int kInKernelMergeMaxPieces = 12;
 // fixed cost is a larger share of each worker's time.
 constexpr int kUnitOverheadSlots = 2;
 constexpr int kUnitOverheadSlotsFew = 4;
-constexpr int kFewTilesPerWorker = 48;
+constexpr int kFewTilesPerWorker = 128;
 inline int unit_overhead_slots(long long tiles, long long workers) {
     return tiles < kFewTilesPerWorker * workers ? kUnitOverheadSlotsFew : kUnitOverheadSlots;
 }
