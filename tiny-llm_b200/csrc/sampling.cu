@@ -34,7 +34,8 @@
 // pass has placed the threshold in a high-byte bin, every CTA lists the slice
 // positions of its keys in that bin and above (up to 4096; more, and the
 // later passes scan the whole slice as before), and the later passes (low
-// bytes of one such bin, the drawn key's count) read only the list. The index
+// bytes of one such bin, the drawn key's count) read only the list, their few
+// keys into one CTA-wide histogram instead of one per warp. The index
 // among equal keys comes from per-CTA counts, a prefix over the cluster's
 // ranks (slices are in index order) and one block-wide scan in the CTA that
 // holds it.
@@ -240,15 +241,26 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
     // sh.gmass / sh.gcnt and their suffix sums: the keys with high byte ==
     // sel (sel < 0: every key), at their high byte (sel < 0) or low byte.
     auto histogram = [&](int sel) {
-        for (int b = lane; b < 256; b += 32) {
-            sh.wlo[warp][b] = 0u;
-            sh.whi[warp][b] = 0u;
-            sh.wcnt[warp][b] = 0u;
-        }
-        __syncwarp();
         // a later pass looks at one bin at or above the threshold bin: the
-        // candidate list holds all of its keys when it did not overflow
+        // candidate list holds all of its keys when it did not overflow, and
+        // its few keys share one histogram (copy 0) instead of one per warp
         const bool from_list = sel >= 0 && use_list;
+        const int hw = from_list ? 0 : warp, ncopies = from_list ? 1 : kWarps;
+        if (from_list) {
+            for (int b = tid; b < 256; b += kThreads) {
+                sh.wlo[0][b] = 0u;
+                sh.whi[0][b] = 0u;
+                sh.wcnt[0][b] = 0u;
+            }
+            __syncthreads();
+        } else {
+            for (int b = lane; b < 256; b += 32) {
+                sh.wlo[warp][b] = 0u;
+                sh.whi[warp][b] = 0u;
+                sh.wcnt[warp][b] = 0u;
+            }
+            __syncwarp();
+        }
         const int cnt_keys = from_list ? ncand : n;
         for (int c = tid; c < cnt_keys; c += kThreads) {
             const int i = from_list ? (int)sh.cand[c] : c;
@@ -261,10 +273,10 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
                 // and more are the keys near the maximum)
                 const u64 x = fx(key);
                 const unsigned xlo = (unsigned)x;
-                const unsigned old = atomicAdd(&sh.wlo[warp][b], xlo);
+                const unsigned old = atomicAdd(&sh.wlo[hw][b], xlo);
                 const unsigned up = (unsigned)(x >> 32) + (old + xlo < old ? 1u : 0u);
-                if (up) atomicAdd(&sh.whi[warp][b], up);
-                atomicAdd(&sh.wcnt[warp][b], 1u);
+                if (up) atomicAdd(&sh.whi[hw][b], up);
+                atomicAdd(&sh.wcnt[hw][b], 1u);
             }
         }
         __syncthreads();
@@ -272,7 +284,7 @@ __global__ void __cluster_dims__(kCtas, 1, 1) __launch_bounds__(kThreads)
         for (int b = tid; b < 256; b += kThreads) {
             u64 ms = 0ull;
             unsigned cs = 0u;
-            for (int w = 0; w < kWarps; ++w) {
+            for (int w = 0; w < ncopies; ++w) {
                 ms += ((u64)sh.whi[w][b] << 32) + sh.wlo[w][b];
                 cs += sh.wcnt[w][b];
             }
